@@ -1,0 +1,1015 @@
+// b2g_gemm.cu — the sm_100a GEMM family C[M,N] = A[M,K] · B[K,N] (fp16/bf16 in, fp32 accumulate) and its C ABI.
+//
+// One persistent, warp-specialised kernel covers the whole config space; tile shape, K step, ring depth, L2 grouping,
+// split-K and operand layout are runtime parameters, so no config needs a compile of its own (the reference compiles
+// one Triton kernel per config, kernels/triton_matmul.py:38-82). Per CTA:
+//   warp 0        TMA producer: loads A/B tiles (128-byte swizzle) into a `stages`-deep shared-memory ring
+//   warp 1        TMEM owner + MMA issuer: tcgen05.mma kind::f16, fp32 accumulators in tensor memory,
+//                 double-buffered when two accumulators fit the 512 TMEM columns
+//   warps 2..     epilogue: tcgen05.ld -> convert -> global store (fp16/bf16 C, or fp32 split-K partials)
+// The tile order follows the reference's grouped-M L2 swizzle (kernels/triton_matmul.py:50-56). SPLIT_K > 1 writes
+// fp32 partials to a [SPLIT_K, M, N] workspace that a second kernel sums in fixed order, so results are bitwise
+// reproducible as in the reference (kernels/triton_matmul.py:6-7, :85-92).
+//
+// Skinny M (BLOCK_M <= 64) swaps the operands: the tensor core's 128-row side runs over N (B^T as the "A" operand,
+// read N-major) and its narrow N side over M, so a 16-row activation still drives full-width MMAs.
+//
+// Every wait on an mbarrier is bounded (%globaltimer); on expiry the kernel records a code in the caller's status
+// word, tells the other roles to stop, drains its own in-flight copies and MMAs, frees tensor memory and returns.
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "b2g.h"
+#include "b2g_ptx.cuh"
+
+#ifndef B2G_SOURCE_HASH
+#define B2G_SOURCE_HASH "unknown"
+#endif
+#define B2G_VERSION_STR "b2g-sm100a-0.1"
+
+namespace b2g {
+
+constexpr int kMaxStages = 16;
+constexpr uint32_t kCtlBytes = 1024;   // control block (barriers, flags) at the start of dynamic shared memory
+constexpr uint32_t kAlignSlack = 1024;  // data ring starts on the next 1024-byte boundary
+constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s per wait: far above any legal stall
+constexpr uint64_t kDrainTimeoutNs = 50000000ull;   // 50 ms to drain in-flight work after an abort
+constexpr size_t kMaxSmemPerCta = 232448;          // sm_100 opt-in maximum dynamic shared memory per block
+
+// control block layout (byte offsets)
+constexpr uint32_t OFF_FULL = 0;      // kMaxStages x u64
+constexpr uint32_t OFF_EMPTY = 128;   // kMaxStages x u64
+constexpr uint32_t OFF_TFULL = 256;   // 2 x u64: accumulator ready for the epilogue
+constexpr uint32_t OFF_TEMPTY = 272;  // 2 x u64: accumulator drained by the epilogue
+constexpr uint32_t OFF_DRAIN = 288;   // u64: all MMAs of this CTA complete
+constexpr uint32_t OFF_TMEM = 296;    // u32: tensor-memory base address written by tcgen05.alloc
+constexpr uint32_t OFF_ABORT = 300;   // u32: set when any role gave up waiting
+
+// status codes written to the caller's device status word
+constexpr int kStatusProducerTimeout = 0x101;
+constexpr int kStatusMmaTimeout = 0x102;
+constexpr int kStatusEpilogueTimeout = 0x103;
+
+enum OutKind : int32_t { OUT_F16 = 0, OUT_BF16 = 1, OUT_F32_PARTIAL = 2 };
+
+// Kernel parameters, in the MMA's orientation: D[i, j] with i over `rows_a` (tensor-memory lanes) and j over
+// `rows_b` (tensor-memory columns). Without the swap i = m, j = n; with it i = n, j = m.
+struct KParams {
+  int32_t rows_a, rows_b, K;
+  int32_t tile_m, tile_n, bk, stages;
+  int32_t group_m, split_k;
+  int32_t tiles_m, tiles_n, num_kb, units;
+  int32_t a_mn_major, b_mn_major;
+  uint32_t idesc;
+  uint32_t a_stage_bytes, b_stage_bytes;
+  uint32_t acc_cols, num_acc, tmem_cols;
+  void* out;
+  int64_t out_si, out_sj, out_split_stride;
+  int32_t out_kind, vec_ok;
+  int* status;
+  uint64_t timeout_ns;
+};
+
+struct Unit {
+  int tm, tn, split, kb0, kb1;
+};
+
+__device__ __forceinline__ Unit decode_unit(const KParams& p, int u) {
+  Unit w;
+  const int t = u / p.split_k;
+  w.split = u - t * p.split_k;
+  const int in_group = p.group_m * p.tiles_n;
+  const int gid = t / in_group;
+  const int first = gid * p.group_m;
+  const int gsz = min(p.tiles_m - first, p.group_m);
+  const int r = t - gid * in_group;
+  w.tm = first + r % gsz;
+  w.tn = r / gsz;
+  w.kb0 = static_cast<int>(static_cast<int64_t>(w.split) * p.num_kb / p.split_k);
+  w.kb1 = static_cast<int>(static_cast<int64_t>(w.split + 1) * p.num_kb / p.split_k);
+  return w;
+}
+
+// Bounded wait: true once the phase with `parity` completed; false if another role aborted or `timeout_ns` passed
+// (then this role sets the abort flag and records `code`).
+__device__ __noinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag, int* status,
+                                        uint64_t timeout_ns, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = 0;
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort_flag) return false;
+      const uint64_t now = global_timer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > timeout_ns) {
+        *abort_flag = 1u;
+        if (status) atomicCAS(status, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+// Wait for a phase during teardown, ignoring the abort flag, for at most `limit_ns`.
+__device__ __noinline__ void drain_phase(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > limit_ns) return;
+  }
+}
+
+__device__ __forceinline__ uint32_t cvt_pair(float a, float b, int bf16) {
+  if (bf16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint16_t cvt_one(float a, int bf16) {
+  if (bf16) {
+    __nv_bfloat16 h = __float2bfloat16_rn(a);
+    return *reinterpret_cast<uint16_t*>(&h);
+  }
+  __half h = __float2half_rn(a);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+
+// Store `ncol` (16 or 32) accumulator values of row i = `row`, columns j = col0.. of D.
+__device__ __forceinline__ void store_chunk(const KParams& p, int split, int64_t row, int64_t col0, int ncol,
+                                            const uint32_t (&v)[32]) {
+  if (row >= p.rows_a) return;
+  const bool full = p.vec_ok && (col0 + ncol <= p.rows_b);
+  if (p.out_kind == OUT_F32_PARTIAL) {
+    float* o = static_cast<float*>(p.out) + static_cast<int64_t>(split) * p.out_split_stride + row * p.out_si;
+    if (full) {
+      float4* dst = reinterpret_cast<float4*>(o + col0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (q * 4 < ncol)
+          dst[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                               __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j < ncol && col0 + j < p.rows_b) o[(col0 + j) * p.out_sj] = __uint_as_float(v[j]);
+      }
+    }
+    return;
+  }
+  const int bf = p.out_kind == OUT_BF16;
+  uint16_t* o = static_cast<uint16_t*>(p.out) + row * p.out_si;
+  if (full) {
+    uint4* dst = reinterpret_cast<uint4*>(o + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (q * 8 < ncol) {
+        uint4 w;
+        w.x = cvt_pair(__uint_as_float(v[8 * q + 0]), __uint_as_float(v[8 * q + 1]), bf);
+        w.y = cvt_pair(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3]), bf);
+        w.z = cvt_pair(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5]), bf);
+        w.w = cvt_pair(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7]), bf);
+        dst[q] = w;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < ncol && col0 + j < p.rows_b) o[(col0 + j) * p.out_sj] = cvt_one(__uint_as_float(v[j]), bf);
+    }
+  }
+}
+
+template <int EPI_WARPS>
+__global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
+    gemm_kernel(const __grid_constant__ KParams p, const __grid_constant__ CUtensorMap tma_a,
+                const __grid_constant__ CUtensorMap tma_b) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t ctl = smem_addr(smem_raw);
+  const uint32_t data = (ctl + kCtlBytes + 1023u) & ~1023u;
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem_raw + OFF_ABORT);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t stage_bytes = p.a_stage_bytes + p.b_stage_bytes;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(ctl + OFF_FULL + 8 * s, 1);
+      mbar_init(ctl + OFF_EMPTY + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(ctl + OFF_TFULL + 8 * b, 1);
+      mbar_init(ctl + OFF_TEMPTY + 8 * b, EPI_WARPS * 32);
+    }
+    mbar_init(ctl + OFF_DRAIN, 1);
+    *abort_flag = 0u;
+    fence_mbar_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(ctl + OFF_TMEM, p.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(smem_raw + OFF_TMEM);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+        const Unit w = decode_unit(p, u);
+        const int row_a = w.tm * p.tile_m;
+        const int row_b = w.tn * p.tile_n;
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!wait_phase(ctl + OFF_EMPTY + 8 * s, ph ^ 1u, abort_flag, p.status, p.timeout_ns,
+                          kStatusProducerTimeout)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full = ctl + OFF_FULL + 8 * s;
+          mbar_arrive_expect_tx(full, stage_bytes);
+          const uint32_t sa = data + s * stage_bytes;
+          const uint32_t sb = sa + p.a_stage_bytes;
+          const int k0 = kb * p.bk;
+          if (p.a_mn_major) {
+            for (int a = 0; a < p.tile_m / 64; ++a)
+              tma_load_2d(sa + a * p.bk * 128, &tma_a, full, row_a + a * 64, k0);
+          } else {
+            for (int a = 0; a < p.bk / 64; ++a) tma_load_2d(sa + a * p.tile_m * 128, &tma_a, full, k0 + a * 64, row_a);
+          }
+          if (p.b_mn_major) {
+            for (int a = 0; a < p.tile_n / 64; ++a)
+              tma_load_2d(sb + a * p.bk * 128, &tma_b, full, row_b + a * 64, k0);
+          } else {
+            for (int a = 0; a < p.bk / 64; ++a) tma_load_2d(sb + a * p.tile_n * 128, &tma_b, full, k0 + a * 64, row_b);
+          }
+          ++issued;
+          if (++s == p.stages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already issued land before the CTA's shared memory is released.
+        const int pending = min(issued, p.stages);
+        int ds = s;
+        uint32_t dph = ph;
+        for (int i = 0; i < pending; ++i) {
+          if (--ds < 0) {
+            ds = p.stages - 1;
+            dph ^= 1u;
+          }
+          drain_phase(ctl + OFF_FULL + 8 * ds, dph, kDrainTimeoutNs);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t acc = 0, acc_ph = 0;
+      bool ok = true;
+      const uint32_t k_atom_a = p.a_mn_major ? 0u : static_cast<uint32_t>(p.tile_m) * 128u;
+      const uint32_t k_atom_b = p.b_mn_major ? 0u : static_cast<uint32_t>(p.tile_n) * 128u;
+      const uint32_t lbo_a = p.a_mn_major ? static_cast<uint32_t>(p.bk) * 128u : 16u;
+      const uint32_t lbo_b = p.b_mn_major ? static_cast<uint32_t>(p.bk) * 128u : 16u;
+      const int ksteps = p.bk / 16;
+      const int halves = p.tile_m / 128;
+      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+        const Unit w = decode_unit(p, u);
+        if (w.kb0 == w.kb1) continue;
+        if (!wait_phase(ctl + OFF_TEMPTY + 8 * acc, acc_ph ^ 1u, abort_flag, p.status, p.timeout_ns,
+                        kStatusMmaTimeout)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_base = tmem_base + acc * p.acc_cols;
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!wait_phase(ctl + OFF_FULL + 8 * s, ph, abort_flag, p.status, p.timeout_ns, kStatusMmaTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = data + s * stage_bytes;
+          const uint32_t sb = sa + p.a_stage_bytes;
+          for (int kk = 0; kk < ksteps; ++kk) {
+            // K offset of this 16-wide step inside the operand tile
+            const uint32_t a_k = p.a_mn_major ? kk * 2048u : (kk >> 2) * k_atom_a + (kk & 3) * 32u;
+            const uint32_t b_k = p.b_mn_major ? kk * 2048u : (kk >> 2) * k_atom_b + (kk & 3) * 32u;
+            const uint64_t bdesc = sdesc_sw128(sb + b_k, lbo_b, 1024u);
+            for (int h = 0; h < halves; ++h) {
+              // rows 128h.. of the A tile: two 64-row atoms on for MN-major, 128 swizzled rows on for K-major
+              const uint32_t a_h = p.a_mn_major ? h * 2u * static_cast<uint32_t>(p.bk) * 128u : h * 128u * 128u;
+              const uint64_t adesc = sdesc_sw128(sa + a_h + a_k, lbo_a, 1024u);
+              umma_f16(d_base + h * p.tile_n, adesc, bdesc, p.idesc, (kb > w.kb0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(ctl + OFF_EMPTY + 8 * s);
+          if (++s == p.stages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(ctl + OFF_TFULL + 8 * acc);
+        if (++acc == p.num_acc) {
+          acc = 0;
+          acc_ph ^= 1u;
+        }
+      }
+      // Every MMA this thread issued has finished before tensor memory is released.
+      umma_commit(ctl + OFF_DRAIN);
+      drain_phase(ctl + OFF_DRAIN, 0, ok ? kWaitTimeoutNs : kDrainTimeoutNs);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int e = warp - 2;
+    const int q = warp & 3;  // tensor-memory lane quarter this warp may access
+    const int grp = e >> 2;
+    constexpr int kGroups = EPI_WARPS / 4;
+    const int nchunks = (p.tile_n + 31) / 32;
+    const int halves = p.tile_m / 128;
+    uint32_t acc = 0, acc_ph = 0;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+      const Unit w = decode_unit(p, u);
+      const bool zero = w.kb0 == w.kb1;
+      if (!zero) {
+        if (!wait_phase(ctl + OFF_TFULL + 8 * acc, acc_ph, abort_flag, p.status, p.timeout_ns,
+                        kStatusEpilogueTimeout))
+          break;
+        tc_fence_after();
+      }
+      for (int h = 0; h < halves; ++h) {
+        const int64_t row = static_cast<int64_t>(w.tm) * p.tile_m + h * 128 + q * 32 + lane;
+        for (int c = grp; c < nchunks; c += kGroups) {
+          const int ncol = min(32, p.tile_n - c * 32);
+          uint32_t v[32];
+          if (zero) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0u;
+          } else {
+            const uint32_t taddr =
+                tmem_base + acc * p.acc_cols + h * p.tile_n + c * 32 + (static_cast<uint32_t>(q * 32) << 16);
+            if (ncol == 32) {
+              tmem_ld_32cols(taddr, v);
+            } else {
+              tmem_ld_16cols(taddr, v);
+            }
+            tmem_ld_wait();
+          }
+          store_chunk(p, w.split, row, static_cast<int64_t>(w.tn) * p.tile_n + c * 32, ncol, v);
+        }
+      }
+      if (!zero) {
+        tc_fence_before();
+        mbar_arrive(ctl + OFF_TEMPTY + 8 * acc);
+        if (++acc == p.num_acc) {
+          acc = 0;
+          acc_ph ^= 1u;
+        }
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, p.tmem_cols);
+  }
+}
+
+// dst[o * ld + i] = src[o * s_outer + i * s_inner] for o < outer, i < inner (2-byte elements). Stages an operand TMA
+// cannot read in place (unaligned leading dimension or arbitrary strides) into a 16-byte-aligned copy.
+__global__ void pack_kernel(const uint16_t* __restrict__ src, int64_t s_outer, int64_t s_inner,
+                            uint16_t* __restrict__ dst, int64_t ld, int64_t outer, int64_t inner) {
+  const int64_t total = outer * inner;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t o = idx / inner;
+    const int64_t i = idx - o * inner;
+    dst[o * ld + i] = src[o * s_outer + i * s_inner];
+  }
+}
+
+// C[m, n] = cast(sum_{s < split} ws[s, m, n]) in increasing s (the reference's fixed-order reduce,
+// kernels/triton_matmul.py:85-92). vec: N % 4 == 0, scn == 1, scm % 4 == 0 and C 8-byte aligned.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ C, int64_t M, int64_t N,
+                                     int64_t scm, int64_t scn, int split, int bf16, int vec) {
+  const int64_t MN = M * N;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  uint16_t* c = static_cast<uint16_t*>(C);
+  if (vec) {
+    for (int64_t q = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; q < MN / 4; q += step) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int s = 0; s < split; ++s) {
+        const float4 x = reinterpret_cast<const float4*>(ws + s * MN)[q];
+        acc.x += x.x;
+        acc.y += x.y;
+        acc.z += x.z;
+        acc.w += x.w;
+      }
+      const int64_t idx = q * 4;
+      const int64_t m = idx / N;
+      const int64_t n = idx - m * N;
+      uint2 w;
+      w.x = cvt_pair(acc.x, acc.y, bf16);
+      w.y = cvt_pair(acc.z, acc.w, bf16);
+      *reinterpret_cast<uint2*>(c + m * scm + n) = w;
+    }
+    return;
+  }
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < MN; idx += step) {
+    float acc = 0.f;
+    for (int s = 0; s < split; ++s) acc += ws[s * MN + idx];
+    const int64_t m = idx / N;
+    const int64_t n = idx - m * N;
+    c[m * scm + n * scn] = cvt_one(acc, bf16);
+  }
+}
+
+}  // namespace b2g
+
+// =====================================================================================================================
+// host side
+// =====================================================================================================================
+using namespace b2g;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int32_t fail(int32_t code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn(std::string& err) {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  static std::string once_err;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || p == nullptr) {
+      once_err = std::string("cuTensorMapEncodeTiled unavailable: ") + cudaGetErrorString(e);
+      return;
+    }
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  err = once_err;
+  return fn;
+}
+
+// One operand of the MMA: element (r, k) at ptr + r*s_r + k*s_k, r < rows (the MN side), k < K.
+struct Operand {
+  const void* src;
+  int64_t rows, K, s_r, s_k;
+  int tile_rows;
+  // decided layout
+  int mn_major;
+  int pack;
+  int64_t ld;   // elements between rows (K-major) or between k (MN-major) of what TMA reads
+  size_t ws_off;  // where the packed copy lives in the workspace
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Decide how TMA reads an operand: in place (K-major or MN-major) or through a packed, 16-byte-strided copy.
+void layout_operand(Operand& o) {
+  int64_t s_r = o.s_r, s_k = o.s_k;
+  if (o.K == 1) s_k = 1;
+  if (o.rows == 1 && s_k != 1) s_r = 1;
+  const bool mn_ok = (o.tile_rows % 64) == 0;
+  o.pack = 0;
+  if (s_k == 1) {
+    const int64_t ld = (o.rows == 1) ? round_up(o.K, 8) : s_r;
+    if (aligned16(o.src) && ld >= o.K && (ld % 8) == 0 && ld < (int64_t(1) << 39)) {
+      o.mn_major = 0;
+      o.ld = ld;
+      return;
+    }
+  }
+  if (s_r == 1 && mn_ok) {
+    const int64_t ld = (o.K == 1) ? round_up(o.rows, 8) : s_k;
+    if (aligned16(o.src) && ld >= o.rows && (ld % 8) == 0 && ld < (int64_t(1) << 39)) {
+      o.mn_major = 1;
+      o.ld = ld;
+      return;
+    }
+  }
+  o.pack = 1;
+  if (s_r == 1 && mn_ok) {  // coalesced copy keeping the MN-contiguous layout
+    o.mn_major = 1;
+    o.ld = round_up(o.rows, 8);
+  } else {
+    o.mn_major = 0;
+    o.ld = round_up(o.K, 8);
+  }
+}
+
+size_t packed_bytes(const Operand& o) {
+  if (!o.pack) return 0;
+  const int64_t outer = o.mn_major ? o.K : o.rows;
+  return static_cast<size_t>(round_up(outer * o.ld * 2, 256));
+}
+
+struct Geometry {
+  bool swapped;
+  int tile_m, tile_n, bk, stages, epi_warps;
+  int tiles_m, tiles_n, num_kb, units;
+  uint32_t acc_cols, num_acc, tmem_cols;
+  size_t smem;
+  Operand a, b;  // MMA "A" (rows over tile_m) and MMA "B" (rows over tile_n)
+  size_t ws_partial;  // split-K partial bytes
+  size_t ws_total;
+};
+
+uint32_t pow2_at_least(uint32_t x) {
+  uint32_t p = 32;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g, const void* A, const void* B) {
+  if (!cfg || !pr) return fail(B2G_ERR_INVALID_ARG, "null config or problem");
+  if (pr->dtype != B2G_DTYPE_F16 && pr->dtype != B2G_DTYPE_BF16)
+    return fail(B2G_ERR_INVALID_ARG, "dtype must be B2G_DTYPE_F16 or B2G_DTYPE_BF16");
+  if (pr->M < 0 || pr->N < 0 || pr->K < 0) return fail(B2G_ERR_INVALID_ARG, "negative dimension");
+  if (pr->M >= (int64_t(1) << 31) || pr->N >= (int64_t(1) << 31) || pr->K >= (int64_t(1) << 31))
+    return fail(B2G_ERR_UNSUPPORTED, "dimension_too_large: each of M, N, K must be < 2^31");
+  const int bm = cfg->block_m, bn = cfg->block_n, bk = cfg->block_k;
+  g.swapped = bm <= 64;
+  if (g.swapped) {
+    if (bm != 16 && bm != 32 && bm != 48 && bm != 64)
+      return fail(B2G_ERR_UNSUPPORTED, "block_m_invalid: skinny BLOCK_M must be 16, 32, 48 or 64");
+    if (bn != 128 && bn != 256)
+      return fail(B2G_ERR_UNSUPPORTED, "block_n_invalid: BLOCK_M <= 64 needs BLOCK_N 128 or 256");
+    g.tile_m = bn;
+    g.tile_n = bm;
+  } else {
+    if (bm != 128 && bm != 256) return fail(B2G_ERR_UNSUPPORTED, "block_m_invalid: BLOCK_M must be <= 64, 128 or 256");
+    if (bn < 16 || bn > 256 || bn % 16 != 0)
+      return fail(B2G_ERR_UNSUPPORTED, "block_n_invalid: BLOCK_N must be a multiple of 16 in [16, 256]");
+    g.tile_m = bm;
+    g.tile_n = bn;
+  }
+  if (bk != 64 && bk != 128) return fail(B2G_ERR_UNSUPPORTED, "block_k_invalid: BLOCK_K must be 64 or 128");
+  if (cfg->num_warps != 4 && cfg->num_warps != 8)
+    return fail(B2G_ERR_UNSUPPORTED, "num_warps_invalid: epilogue warps must be 4 or 8");
+  if (cfg->num_stages < 2 || cfg->num_stages > kMaxStages)
+    return fail(B2G_ERR_UNSUPPORTED, "num_stages_invalid: stages must be in [2, 16]");
+  if (cfg->group_m < 1) return fail(B2G_ERR_UNSUPPORTED, "group_m_invalid: GROUP_M must be >= 1");
+  if (cfg->split_k < 1 || cfg->split_k > 64) return fail(B2G_ERR_UNSUPPORTED, "split_k_invalid: SPLIT_K in [1, 64]");
+  if (cfg->schedule != B2G_SCHED_PERSISTENT && cfg->schedule != B2G_SCHED_TILE)
+    return fail(B2G_ERR_UNSUPPORTED, "schedule_invalid");
+  g.bk = bk;
+  g.stages = cfg->num_stages;
+  g.epi_warps = cfg->num_warps;
+
+  const int64_t M = pr->M, N = pr->N, K = pr->K;
+  // operands in MMA orientation
+  Operand oa{}, ob{};
+  if (!g.swapped) {
+    oa = Operand{A, M, K, pr->stride_am, pr->stride_ak, g.tile_m, 0, 0, 0, 0};
+    ob = Operand{B, N, K, pr->stride_bn, pr->stride_bk, g.tile_n, 0, 0, 0, 0};
+  } else {
+    oa = Operand{B, N, K, pr->stride_bn, pr->stride_bk, g.tile_m, 0, 0, 0, 0};
+    ob = Operand{A, M, K, pr->stride_am, pr->stride_ak, g.tile_n, 0, 0, 0, 0};
+  }
+  layout_operand(oa);
+  layout_operand(ob);
+  g.a = oa;
+  g.b = ob;
+  const int64_t rows_a = g.swapped ? N : M;
+  const int64_t rows_b = g.swapped ? M : N;
+  g.tiles_m = static_cast<int>((rows_a + g.tile_m - 1) / g.tile_m);
+  g.tiles_n = static_cast<int>((rows_b + g.tile_n - 1) / g.tile_n);
+  g.num_kb = static_cast<int>((K + bk - 1) / bk);
+  const int64_t units = static_cast<int64_t>(g.tiles_m) * g.tiles_n * cfg->split_k;
+  if (units >= (int64_t(1) << 31)) return fail(B2G_ERR_UNSUPPORTED, "too_many_tiles");
+  g.units = static_cast<int>(units);
+  g.acc_cols = static_cast<uint32_t>(g.tile_m / 128 * g.tile_n);
+  g.num_acc = (2 * g.acc_cols <= 512) ? 2u : 1u;
+  g.tmem_cols = pow2_at_least(g.num_acc * g.acc_cols);
+  const size_t stage = static_cast<size_t>(g.tile_m + g.tile_n) * bk * 2;
+  g.smem = kCtlBytes + kAlignSlack + stage * g.stages;
+  if (g.smem > kMaxSmemPerCta) return fail(B2G_ERR_UNSUPPORTED, "smem_exceeds_limit");
+  const int64_t ws_elems = static_cast<int64_t>(cfg->split_k) * M * N;
+  if (cfg->split_k > 1 && ws_elems >= (int64_t(1) << 40))
+    return fail(B2G_ERR_UNSUPPORTED, "split_k_workspace_too_large");
+  g.ws_partial = cfg->split_k > 1 ? static_cast<size_t>(round_up(ws_elems * 4, 256)) : 0;
+  g.a.ws_off = g.ws_partial;
+  g.b.ws_off = g.a.ws_off + packed_bytes(g.a);
+  g.ws_total = g.b.ws_off + packed_bytes(g.b);
+  return B2G_OK;
+}
+
+struct DeviceInit {
+  std::once_flag flag;
+  cudaError_t err = cudaSuccess;
+  int sm_count = 0;
+};
+DeviceInit g_dev[64];
+
+int32_t init_device(int dev, int& sm_count) {
+  if (dev < 0 || dev >= 64) return fail(B2G_ERR_CUDA, "device index out of range");
+  DeviceInit& d = g_dev[dev];
+  std::call_once(d.flag, [&d, dev] {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kMaxSmemPerCta));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kMaxSmemPerCta));
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    d.err = e;
+  });
+  if (d.err != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("device set-up: ") + cudaGetErrorString(d.err));
+  sm_count = d.sm_count;
+  return B2G_OK;
+}
+
+int32_t encode_operand(const Operand& o, const void* base, int dtype, int bk, CUtensorMap* map) {
+  std::string err;
+  EncodeTiledFn enc = get_encode_fn(err);
+  if (!enc) return fail(B2G_ERR_CUDA, err);
+  const CUtensorMapDataType dt = dtype == B2G_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2];
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(o.ld) * 2};
+  cuuint32_t box[2];
+  cuuint32_t estr[2] = {1, 1};
+  if (o.mn_major) {
+    dims[0] = static_cast<cuuint64_t>(o.rows);
+    dims[1] = static_cast<cuuint64_t>(o.K);
+    box[0] = 64;
+    box[1] = static_cast<cuuint32_t>(bk);
+  } else {
+    dims[0] = static_cast<cuuint64_t>(o.K);
+    dims[1] = static_cast<cuuint64_t>(o.rows);
+    box[0] = 64;
+    box[1] = static_cast<cuuint32_t>(o.tile_rows);
+  }
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[256];
+    snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu, ld %lld, box %u x %u", (int)r,
+             (unsigned long long)dims[0], (unsigned long long)dims[1], (long long)o.ld, box[0], box[1]);
+    return fail(B2G_ERR_CUDA, buf);
+  }
+  return B2G_OK;
+}
+
+}  // namespace
+
+struct b2g_plan {
+  int device;
+  int empty;       // M == 0 or N == 0: nothing to launch
+  int k_zero;      // K == 0: only the zero fill
+  KParams kp;
+  CUtensorMap tma_a, tma_b;
+  int epi_warps;
+  int grid, threads;
+  size_t smem;
+  // packing
+  int pack_a, pack_b;
+  const void* pa_src;
+  int64_t pa_so, pa_si, pa_ld, pa_outer, pa_inner;
+  void* pa_dst;
+  const void* pb_src;
+  int64_t pb_so, pb_si, pb_ld, pb_outer, pb_inner;
+  void* pb_dst;
+  // split-K reduce
+  int reduce;
+  const float* r_ws;
+  void* r_c;
+  int64_t r_M, r_N, r_scm, r_scn;
+  int r_split, r_bf16, r_vec;
+};
+
+namespace {
+
+void fill_pack(const Operand& o, void* ws, const void*& src, int64_t& so, int64_t& si, int64_t& ld, int64_t& outer,
+               int64_t& inner, void*& dst) {
+  src = o.src;
+  dst = static_cast<uint8_t*>(ws) + o.ws_off;
+  ld = o.ld;
+  if (o.mn_major) {
+    outer = o.K;
+    inner = o.rows;
+    so = o.s_k;
+    si = o.s_r;
+  } else {
+    outer = o.rows;
+    inner = o.K;
+    so = o.s_r;
+    si = o.s_k;
+  }
+}
+
+int grid_for(int64_t work, int per_block) {
+  int64_t g = (work + per_block - 1) / per_block;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(g, 148 * 16)));
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t b2g_abi_version(void) { return B2G_ABI_VERSION; }
+const char* b2g_version(void) { return B2G_VERSION_STR; }
+const char* b2g_source_hash(void) { return B2G_SOURCE_HASH; }
+const char* b2g_last_error(void) { return g_last_error.c_str(); }
+
+const char* b2g_error_string(int32_t code) {
+  switch (code) {
+    case B2G_OK: return "ok";
+    case B2G_ERR_INVALID_ARG: return "invalid argument";
+    case B2G_ERR_UNSUPPORTED: return "unsupported configuration";
+    case B2G_ERR_WORKSPACE: return "workspace missing or too small";
+    case B2G_ERR_CUDA: return "CUDA error";
+    default: return "unknown error";
+  }
+}
+
+const char* b2g_status_string(int32_t status) {
+  switch (status) {
+    case 0: return "ok";
+    case kStatusProducerTimeout: return "device wait timed out in the TMA producer";
+    case kStatusMmaTimeout: return "device wait timed out in the MMA issuer";
+    case kStatusEpilogueTimeout: return "device wait timed out in the epilogue";
+    default: return "unknown device status";
+  }
+}
+
+int32_t b2g_check(const b2g_config* cfg, const b2g_problem* prob, char* reason, size_t reason_len) {
+  Geometry g;
+  // alignment of the real pointers is unknown here: assume 16-byte aligned bases (packing covers the rest)
+  int32_t rc = make_geometry(cfg, prob, g, reinterpret_cast<const void*>(256), reinterpret_cast<const void*>(256));
+  if (rc != B2G_OK && reason && reason_len) {
+    strncpy(reason, g_last_error.c_str(), reason_len - 1);
+    reason[reason_len - 1] = 0;
+  } else if (reason && reason_len) {
+    reason[0] = 0;
+  }
+  return rc;
+}
+
+int32_t b2g_workspace_size(const b2g_config* cfg, const b2g_problem* prob, const void* A, const void* B,
+                           size_t* bytes) {
+  if (!bytes) return fail(B2G_ERR_INVALID_ARG, "null bytes");
+  Geometry g;
+  const void* dflt = reinterpret_cast<const void*>(256);
+  int32_t rc = make_geometry(cfg, prob, g, A ? A : dflt, B ? B : dflt);
+  if (rc != B2G_OK) return rc;
+  *bytes = g.ws_total;
+  return B2G_OK;
+}
+
+int32_t b2g_smem_bytes(const b2g_config* cfg, const b2g_problem* prob, size_t* bytes) {
+  if (!bytes) return fail(B2G_ERR_INVALID_ARG, "null bytes");
+  Geometry g;
+  int32_t rc = make_geometry(cfg, prob, g, reinterpret_cast<const void*>(256), reinterpret_cast<const void*>(256));
+  if (rc != B2G_OK && rc != B2G_ERR_UNSUPPORTED) return rc;
+  const size_t stage = static_cast<size_t>((cfg->block_m <= 64 ? cfg->block_n + cfg->block_m : cfg->block_m + cfg->block_n)) *
+                       cfg->block_k * 2;
+  *bytes = kCtlBytes + kAlignSlack + stage * cfg->num_stages;
+  return B2G_OK;
+}
+
+int32_t b2g_plan_create(const b2g_config* cfg, const b2g_problem* prob, const void* A, const void* B, void* C,
+                        void* workspace, size_t workspace_bytes, int32_t* status, b2g_plan** out) {
+  if (!out) return fail(B2G_ERR_INVALID_ARG, "null plan output");
+  *out = nullptr;
+  Geometry g;
+  int32_t rc = make_geometry(cfg, prob, g, A, B);
+  if (rc != B2G_OK) return rc;
+  const int64_t M = prob->M, N = prob->N, K = prob->K;
+  if ((M > 0 && N > 0) && (!C || (K > 0 && (!A || !B)))) return fail(B2G_ERR_INVALID_ARG, "null A, B or C");
+  if (g.ws_total > 0 && (workspace == nullptr || workspace_bytes < g.ws_total)) {
+    char buf[160];
+    snprintf(buf, sizeof buf, "workspace of %zu bytes needed, %zu given", g.ws_total,
+             workspace == nullptr ? size_t(0) : workspace_bytes);
+    return fail(B2G_ERR_WORKSPACE, buf);
+  }
+  if (g.ws_total > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(B2G_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return fail(B2G_ERR_CUDA, cudaGetErrorString(ce));
+  int sm_count = 0;
+  rc = init_device(dev, sm_count);
+  if (rc != B2G_OK) return rc;
+
+  b2g_plan* p = new b2g_plan();
+  memset(p, 0, sizeof(*p));
+  p->device = dev;
+  p->empty = (M == 0 || N == 0);
+  p->k_zero = (K == 0);
+  const int bf16 = prob->dtype == B2G_DTYPE_BF16;
+  if (!p->empty && p->k_zero) {
+    p->reduce = 1;
+    p->r_ws = nullptr;
+    p->r_c = C;
+    p->r_M = M;
+    p->r_N = N;
+    p->r_scm = prob->stride_cm;
+    p->r_scn = prob->stride_cn;
+    p->r_split = 0;
+    p->r_bf16 = bf16;
+    p->r_vec = 0;
+  }
+  if (!p->empty && !p->k_zero) {
+    const void* a_base = g.a.src;
+    const void* b_base = g.b.src;
+    if (g.a.pack) {
+      p->pack_a = 1;
+      fill_pack(g.a, workspace, p->pa_src, p->pa_so, p->pa_si, p->pa_ld, p->pa_outer, p->pa_inner, p->pa_dst);
+      a_base = p->pa_dst;
+    }
+    if (g.b.pack) {
+      p->pack_b = 1;
+      fill_pack(g.b, workspace, p->pb_src, p->pb_so, p->pb_si, p->pb_ld, p->pb_outer, p->pb_inner, p->pb_dst);
+      b_base = p->pb_dst;
+    }
+    rc = encode_operand(g.a, a_base, prob->dtype, g.bk, &p->tma_a);
+    if (rc == B2G_OK) rc = encode_operand(g.b, b_base, prob->dtype, g.bk, &p->tma_b);
+    if (rc != B2G_OK) {
+      delete p;
+      return rc;
+    }
+    KParams& k = p->kp;
+    k.rows_a = static_cast<int32_t>(g.swapped ? N : M);
+    k.rows_b = static_cast<int32_t>(g.swapped ? M : N);
+    k.K = static_cast<int32_t>(K);
+    k.tile_m = g.tile_m;
+    k.tile_n = g.tile_n;
+    k.bk = g.bk;
+    k.stages = g.stages;
+    k.group_m = cfg->group_m;
+    k.split_k = cfg->split_k;
+    k.tiles_m = g.tiles_m;
+    k.tiles_n = g.tiles_n;
+    k.num_kb = g.num_kb;
+    k.units = g.units;
+    k.a_mn_major = g.a.mn_major;
+    k.b_mn_major = g.b.mn_major;
+    k.idesc = idesc_f16(bf16 ? 1u : 0u, static_cast<uint32_t>(g.a.mn_major), static_cast<uint32_t>(g.b.mn_major),
+                        128u, static_cast<uint32_t>(g.tile_n));
+    k.a_stage_bytes = static_cast<uint32_t>(g.tile_m * g.bk * 2);
+    k.b_stage_bytes = static_cast<uint32_t>(g.tile_n * g.bk * 2);
+    k.acc_cols = g.acc_cols;
+    k.num_acc = g.num_acc;
+    k.tmem_cols = g.tmem_cols;
+    k.status = status;
+    k.timeout_ns = kWaitTimeoutNs;
+    if (cfg->split_k > 1) {
+      k.out = workspace;
+      k.out_kind = OUT_F32_PARTIAL;
+      k.out_split_stride = M * N;
+      k.out_si = g.swapped ? 1 : N;
+      k.out_sj = g.swapped ? N : 1;
+      k.vec_ok = (k.out_sj == 1) && (k.out_si % 4 == 0);
+      p->reduce = 1;
+      p->r_ws = static_cast<const float*>(workspace);
+      p->r_c = C;
+      p->r_M = M;
+      p->r_N = N;
+      p->r_scm = prob->stride_cm;
+      p->r_scn = prob->stride_cn;
+      p->r_split = cfg->split_k;
+      p->r_bf16 = bf16;
+      p->r_vec = (N % 4 == 0) && prob->stride_cn == 1 && (prob->stride_cm % 4 == 0) &&
+                 ((reinterpret_cast<uintptr_t>(C) & 7u) == 0);
+    } else {
+      k.out = C;
+      k.out_kind = bf16 ? OUT_BF16 : OUT_F16;
+      k.out_split_stride = 0;
+      k.out_si = g.swapped ? prob->stride_cn : prob->stride_cm;
+      k.out_sj = g.swapped ? prob->stride_cm : prob->stride_cn;
+      k.vec_ok = (k.out_sj == 1) && (k.out_si % 8 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+    }
+    p->epi_warps = g.epi_warps;
+    p->threads = (2 + g.epi_warps) * 32;
+    p->smem = g.smem;
+    int64_t grid = g.units;
+    if (cfg->schedule == B2G_SCHED_PERSISTENT) {
+      int occ = 0;
+      ce = (g.epi_warps == 4)
+               ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_kernel<4>, p->threads, p->smem)
+               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_kernel<8>, p->threads, p->smem);
+      if (ce != cudaSuccess) {
+        delete p;
+        return fail(B2G_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(ce));
+      }
+      occ = std::max(1, std::min<int>(occ, static_cast<int>(512 / g.tmem_cols)));
+      grid = std::min<int64_t>(grid, static_cast<int64_t>(sm_count) * occ);
+    }
+    p->grid = static_cast<int>(std::max<int64_t>(grid, 1));
+  }
+  *out = p;
+  return B2G_OK;
+}
+
+int32_t b2g_plan_launch(const b2g_plan* p, void* stream) {
+  if (!p) return fail(B2G_ERR_INVALID_ARG, "null plan");
+  if (p->empty) return B2G_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p->pack_a) {
+    pack_kernel<<<grid_for(p->pa_outer * p->pa_inner, 256), 256, 0, st>>>(
+        static_cast<const uint16_t*>(p->pa_src), p->pa_so, p->pa_si, static_cast<uint16_t*>(p->pa_dst), p->pa_ld,
+        p->pa_outer, p->pa_inner);
+  }
+  if (p->pack_b) {
+    pack_kernel<<<grid_for(p->pb_outer * p->pb_inner, 256), 256, 0, st>>>(
+        static_cast<const uint16_t*>(p->pb_src), p->pb_so, p->pb_si, static_cast<uint16_t*>(p->pb_dst), p->pb_ld,
+        p->pb_outer, p->pb_inner);
+  }
+  if (!p->k_zero) {
+    if (p->epi_warps == 4) {
+      gemm_kernel<4><<<p->grid, p->threads, p->smem, st>>>(p->kp, p->tma_a, p->tma_b);
+    } else {
+      gemm_kernel<8><<<p->grid, p->threads, p->smem, st>>>(p->kp, p->tma_a, p->tma_b);
+    }
+  }
+  if (p->reduce) {
+    const int64_t work = p->r_vec ? p->r_M * p->r_N / 4 : p->r_M * p->r_N;
+    splitk_reduce_kernel<<<grid_for(work, 256), 256, 0, st>>>(p->r_ws, p->r_c, p->r_M, p->r_N, p->r_scm, p->r_scn,
+                                                                p->r_split, p->r_bf16, p->r_vec);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
+  return B2G_OK;
+}
+
+int32_t b2g_plan_num_kernels(const b2g_plan* p) {
+  if (!p || p->empty) return 0;
+  return p->pack_a + p->pack_b + (p->k_zero ? 0 : 1) + p->reduce;
+}
+
+int32_t b2g_plan_grid(const b2g_plan* p) { return p ? p->grid : 0; }
+
+int32_t b2g_plan_destroy(b2g_plan* p) {
+  delete p;
+  return B2G_OK;
+}
+
+int32_t b2g_gemm(const b2g_config* cfg, const b2g_problem* prob, const void* A, const void* B, void* C,
+                 void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  b2g_plan* p = nullptr;
+  int32_t rc = b2g_plan_create(cfg, prob, A, B, C, workspace, workspace_bytes, status, &p);
+  if (rc != B2G_OK) return rc;
+  rc = b2g_plan_launch(p, stream);
+  b2g_plan_destroy(p);
+  return rc;
+}
+
+int32_t b2g_splitk_reduce(const float* ws, void* C, int64_t M, int64_t N, int64_t stride_cm, int64_t stride_cn,
+                          int32_t split, int32_t dtype, void* stream) {
+  if (M < 0 || N < 0 || split < 0) return fail(B2G_ERR_INVALID_ARG, "negative size");
+  if (dtype != B2G_DTYPE_F16 && dtype != B2G_DTYPE_BF16) return fail(B2G_ERR_INVALID_ARG, "bad dtype");
+  if (M == 0 || N == 0) return B2G_OK;
+  if (!C || (split > 0 && !ws)) return fail(B2G_ERR_INVALID_ARG, "null pointer");
+  const int vec = (N % 4 == 0) && stride_cn == 1 && (stride_cm % 4 == 0) &&
+                  ((reinterpret_cast<uintptr_t>(C) & 7u) == 0) && ((reinterpret_cast<uintptr_t>(ws) & 15u) == 0);
+  const int64_t work = vec ? M * N / 4 : M * N;
+  splitk_reduce_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      ws, C, M, N, stride_cm, stride_cn, split, dtype == B2G_DTYPE_BF16, vec);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
+  return B2G_OK;
+}
+
+}  // extern "C"

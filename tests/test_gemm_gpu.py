@@ -1,0 +1,197 @@
+"""GPU parity tests: the sm_100a family, called through the C ABI, against the CPU oracle.
+
+Ported in spirit from the reference's tests/test_kernels.py (hand-picked configs x its 8 shapes, split-K with uneven K,
+bitwise split-K determinism, bf16) and tests/test_correctness.py (NaN-prefilled outputs, so unwritten elements fail).
+Every result must pass both bounds, written here:
+  * the reference's gate (tune/correctness.py:116-127): |C-ref| <= 1e-2*|ref| + 1e-2*sqrt(K) (bf16: 3e-2, 3e-2);
+  * the north star's per-element bound: |C-ref|_ij <= 2e-3 * ||A_i,:||_2 * ||B_:,j||_2.
+"""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from cs464_b200.config_space import HANDPICKED, shape_violations
+from cs464_b200.matmul import B200Matmul, MatmulConfig
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+# the reference's kernel-test shapes (tests/test_kernels.py:10-11)
+SHAPES = [(1, 1, 1), (1, 4096, 4096), (17, 33, 65), (128, 128, 128), (129, 257, 1031), (513, 255, 16),
+          (2048, 2048, 8), (64, 64, 16384)]
+
+
+def _run(cfg, a_cpu, b_cpu, *, a_dev=None, b_dev=None):
+    """Run `cfg` on the operands (copied to the GPU unless device views are given) into a NaN-filled output."""
+    a = a_dev if a_dev is not None else a_cpu.cuda()
+    b = b_dev if b_dev is not None else b_cpu.cuda()
+    out = torch.full((a.shape[0], b.shape[1]), float("nan"), device=a.device, dtype=a.dtype)
+    run = B200Matmul(cfg).make_runner(a, b, out=out)
+    c = run()
+    torch.cuda.synchronize()
+    run.raise_on_status()
+    assert c.data_ptr() == out.data_ptr()
+    return c, run
+
+
+def _assert_parity(c, ref, a_cpu, b_cpu, K):
+    c32 = c.float().cpu().numpy()
+    dt = "bfloat16" if c.dtype == torch.bfloat16 else "float16"
+    r = oracle.check_output(c32, ref, K, dt)
+    assert r.valid, r
+    ok, worst = oracle.norm_rel_check(c32, ref, a_cpu, b_cpu)
+    assert ok, f"norm-relative error {worst:.3e} > {oracle.NORM_REL_TOL}"
+    return worst
+
+
+@pytest.mark.parametrize("name", list(HANDPICKED))
+@pytest.mark.parametrize("shape", SHAPES)
+def test_handpicked_matches_oracle(name, shape):
+    cfg = HANDPICKED[name]
+    M, N, K = shape
+    if "split_k_workspace_too_large" in shape_violations(cfg, M, N, K):
+        pytest.skip("workspace limit")
+    a, b = oracle.make_inputs(M, N, K, seed=0)
+    ref = oracle.gemm_f32(a, b)
+    c, _ = _run(cfg, a, b)
+    _assert_parity(c, ref, a, b, K)
+
+
+@pytest.mark.parametrize("case", json.loads((GOLDEN / "gemm_cases.json").read_text())["cases"], ids=lambda c: c["name"])
+@pytest.mark.parametrize("name", ["large_square", "skinny_m", "large_k_splitk"])
+def test_golden_cases(case, name):
+    """The reference's own fp32 results (tests/golden, made by running tune/correctness.py) as the oracle."""
+    z = np.load(GOLDEN / "gemm_cases.npz")
+    dt = torch.bfloat16 if case["dtype"] == "bfloat16" else torch.float16
+    a = torch.from_numpy(z[f"{case['name']}_a"].view(np.int16)).view(dt)
+    b = torch.from_numpy(z[f"{case['name']}_b"].view(np.int16)).view(dt)
+    ref = z[f"{case['name']}_ref"]
+    cfg = HANDPICKED[name]
+    c, _ = _run(cfg, a, b)
+    _assert_parity(c, ref, a, b, case["K"])
+
+
+@pytest.mark.parametrize("split_k", [2, 4, 16])
+@pytest.mark.parametrize("bm", [128, 16])
+def test_split_k_uneven_k(split_k, bm):
+    cfg = MatmulConfig(bm, 128 if bm < 128 else 64, 64, num_warps=4, num_stages=4, GROUP_M=1, SPLIT_K=split_k)
+    a, b = oracle.make_inputs(100, 70, 1000, seed=0)
+    c, _ = _run(cfg, a, b)
+    _assert_parity(c, oracle.gemm_f32(a, b), a, b, 1000)
+
+
+def test_split_k_deterministic():
+    cfg = MatmulConfig(128, 128, 64, SPLIT_K=8)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(256, 4096, device="cuda", generator=g).half()
+    b = torch.randn(4096, 256, device="cuda", generator=g).half()
+    run = B200Matmul(cfg).make_runner(a, b)
+    c1 = run().clone()
+    c2 = run().clone()
+    assert torch.equal(c1, c2)
+
+
+@pytest.mark.parametrize("name", ["medium", "skinny_m", "large_k_splitk"])
+def test_bf16(name):
+    a, b = oracle.make_inputs(300, 200, 500, dtype=torch.bfloat16, seed=0)
+    c, _ = _run(HANDPICKED[name], a, b)
+    _assert_parity(c, oracle.gemm_f32(a, b), a, b, 500)
+
+
+@pytest.mark.parametrize("cfg", [
+    MatmulConfig(128, 128, 64, num_stages=4),
+    MatmulConfig(256, 128, 64, num_stages=4),
+    MatmulConfig(128, 256, 128, num_stages=2, num_warps=8),
+    MatmulConfig(256, 256, 64, num_stages=3, num_warps=8),
+    MatmulConfig(128, 192, 64, num_stages=4),
+    MatmulConfig(32, 256, 64, num_stages=4, GROUP_M=1),
+    MatmulConfig(64, 128, 128, num_stages=4, GROUP_M=1),
+    MatmulConfig(48, 128, 64, num_stages=4, GROUP_M=1),
+    MatmulConfig(128, 128, 64, num_stages=4, PERSISTENT=0),
+    MatmulConfig(128, 64, 128, num_stages=4, GROUP_M=4, SPLIT_K=3),
+], ids=lambda c: c.key())
+@pytest.mark.parametrize("shape", [(300, 520, 700), (1024, 1024, 1024), (40, 1000, 3000)])
+def test_knobs_match_oracle(cfg, shape):
+    M, N, K = shape
+    a, b = oracle.make_inputs(M, N, K, seed=1)
+    c, _ = _run(cfg, a, b)
+    _assert_parity(c, oracle.gemm_f32(a, b), a, b, K)
+
+
+@pytest.mark.parametrize("layout", ["a_t", "b_t", "both_t", "a_offset", "b_strided"])
+@pytest.mark.parametrize("name", ["medium", "skinny_m"])
+def test_layouts(layout, name):
+    """Transposed views read MN-major or K-major in place; unaligned views go through the packing kernel."""
+    M, N, K = 200, 256, 320
+    a, b = oracle.make_inputs(M, N, K, seed=2)
+    a_dev, b_dev = a.cuda(), b.cuda()
+    if layout in ("a_t", "both_t"):
+        a_dev = a_dev.t().contiguous().t()  # stride (1, M)
+    if layout in ("b_t", "both_t"):
+        b_dev = b_dev.t().contiguous().t()  # stride (1, K)
+    if layout == "a_offset":
+        buf = torch.empty(M * K + 1, device="cuda", dtype=a.dtype)
+        a_dev = buf[1:].view(M, K)  # base 2 bytes off 16-byte alignment
+        a_dev.copy_(a.cuda())
+    if layout == "b_strided":
+        buf = torch.empty(K, N * 2, device="cuda", dtype=b.dtype)
+        b_dev = buf[:, ::2]  # stride (2N, 2)
+        b_dev.copy_(b.cuda())
+    c, _ = _run(HANDPICKED[name], a, b, a_dev=a_dev, b_dev=b_dev)
+    _assert_parity(c, oracle.gemm_f32(a, b), a, b, K)
+
+
+def test_empty_and_k_zero():
+    cfg = HANDPICKED["medium"]
+    a = torch.empty(0, 64, device="cuda", dtype=torch.float16)
+    b = torch.empty(64, 32, device="cuda", dtype=torch.float16)
+    assert B200Matmul(cfg).make_runner(a, b)().shape == (0, 32)
+    a = torch.empty(5, 0, device="cuda", dtype=torch.float16)
+    b = torch.empty(0, 7, device="cuda", dtype=torch.float16)
+    c, _ = _run(cfg, a.cpu(), b.cpu())
+    assert torch.equal(c, torch.zeros(5, 7, device="cuda", dtype=torch.float16))
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096, 4096), (8192, 8192, 1024), (2048, 28672, 4096)])
+def test_large_vs_cpu_reference(shape):
+    """Large shapes against the reference's fp32 reference run on the host (torch CPU, all threads)."""
+    M, N, K = shape
+    a, b = oracle.make_inputs(M, N, K, seed=0)
+    ref = oracle.reference_cpu(a, b).numpy()
+    c, _ = _run(HANDPICKED["large_square"], a, b)
+    _assert_parity(c, ref, a, b, K)
+
+
+def test_square_16384_properties():
+    """At the largest square size: every config family agrees with the fp32 GPU reference within the bound, and
+    split-K is bitwise stable run to run."""
+    M = N = K = 16384
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(M, K, device="cuda", generator=g).half()
+    b = torch.randn(K, N, device="cuda", generator=g).half()
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = a.float() @ b.float()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    an = a.float().norm(dim=1)
+    bn = b.float().norm(dim=0)
+    for cfg in (HANDPICKED["large_square"], MatmulConfig(256, 256, 64, num_stages=3, num_warps=8),
+                MatmulConfig(128, 128, 64, num_stages=6, SPLIT_K=2)):
+        run = B200Matmul(cfg).make_runner(a, b)
+        c = run()
+        torch.cuda.synchronize()
+        run.raise_on_status()
+        err = (c.float() - ref).abs()
+        ratio = float((err / (an[:, None] * bn[None, :])).max())
+        assert ratio <= oracle.NORM_REL_TOL, (cfg.key(), ratio)
+        if cfg.SPLIT_K > 1:
+            assert torch.equal(c, run())
+        del c, err

@@ -1,0 +1,325 @@
+#!/usr/bin/env python
+"""Headline benchmark: fp16 GEMM TFLOP/s of the sm_100a family on BASELINE.json configs[1], the square sweep.
+
+Workload: M = N = K in {256, 512, 1024, 2048, 4096, 8192, 16384}, row-major A[M,K] and B[K,N] with i.i.d. N(0,1)
+entries cast to fp16 (CUDA generator, seed 0), fp32 accumulate, fp16 output. One step = one GEMM of every size, each
+preceded by an L2 flush (a 1 GiB write, outside the GEMM's timed interval). `value` = sum of 2*n^3 over the sizes, all
+steps and all ranks, divided by the summed device time of the GEMMs (CUDA events on the launching stream, max over
+ranks). Each size runs the config the shipped zero-search rule (cs464_b200.select) or the winner cache picks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+With N > 1 (torchrun, one process per GPU) every rank runs the whole sweep on its own GPU: a GEMM does not shard,
+so the ranks are replicas ("scaling": "weak"); the process group only carries the barrier and the max-reduction
+of the timings.
+
+`--impl reference` times the reference's CPU path for the same metric: the fp32 `a.float() @ b.float()` of
+tune/correctness.py:100-102 (the CPU oracle's restatement, oracle.reference_cpu) on the host cores, all threads,
+over a bounded sample of the sweep (sizes up to 2048 per step).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SIZES = [256, 512, 1024, 2048, 4096, 8192, 16384]
+CPU_SAMPLE_SIZES = [256, 512, 1024, 2048]
+METRIC = "fp16 GEMM TFLOP/s (% of B200 dense peak)"
+UNIT = "TFLOP/s"
+FALLBACK_PEAK_TFLOPS = 1590.0
+FLUSH_BYTES = 1 << 30
+# DRAM bytes (read + write) of one 16384^3 launch of the dominant kernel, scaled from an ncu capture of a smaller case;
+# see profiles/ for the capture and the scaling. None until measured.
+TRAFFIC_BYTES_16384 = None
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--sizes", type=str, default=None, help="comma-separated square sizes (default: the full sweep)")
+    ap.add_argument("--config", type=str, default=None, help="force one config key for every size")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    a = ap.parse_args()
+    if a.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    return a
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def measured_peaks() -> tuple[float, str, float | None]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)", float(d.get("hbm_gbs"))
+    except (OSError, ValueError, KeyError, TypeError):
+        return FALLBACK_PEAK_TFLOPS, "fallback (1.59 PFLOP/s, earlier measurement on this pool)", None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling of this process's GPU during the timed region."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="clocks_", suffix=".csv")[1])
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9 or (self.uuid and self.uuid not in parts[0]):
+                continue
+            rows.append(parts)
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        power = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(power) if power else None}
+
+
+def cpu_reference(sizes, steps: int, warmup: int, budget_s: float | None = None):
+    """The reference's CPU path (fp32 matmul of the upcast fp16 inputs, all host threads) over `sizes` per step.
+    Returns (TFLOP/s, seconds per step, threads, sample description)."""
+    import torch
+
+    from oracle import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    inputs = [oracle.make_inputs(n, n, n, seed=0) for n in sizes]
+    flops = sum(2.0 * n ** 3 for n in sizes)
+    for _ in range(warmup):
+        for a, b in inputs:
+            oracle.reference_cpu(a, b)
+    times = []
+    t_all = time.perf_counter()
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        for a, b in inputs:
+            oracle.reference_cpu(a, b)
+        times.append(time.perf_counter() - t0)
+        if budget_s is not None and time.perf_counter() - t_all > budget_s:
+            break
+    sec = statistics.median(times)
+    sample = f"square sizes {sizes} (fp16 inputs upcast to fp32, torch CPU matmul), {len(times)} timed steps"
+    return flops / sec / 1e12, sec, torch.get_num_threads(), sample
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    sizes = [n for n in (args.sizes_list or SIZES) if n <= max(CPU_SAMPLE_SIZES)]
+    tflops, sec, threads, sample = cpu_reference(sizes, args.steps, args.warmup)
+    line = {"metric": METRIC, "value": round(tflops, 4), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic", "impl": "reference",
+            "config": workload_config(args),
+            "cpu_baseline": {"value": round(tflops, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(tflops, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args) -> dict:
+    return {"workload": "square_sweep_fp16 (BASELINE.json configs[1])", "sizes": args.sizes_list or SIZES,
+            "inputs": "N(0,1) cast to fp16, seed 0", "layout": "row-major NN, fp32 accumulate, fp16 out",
+            "l2": "flushed before every GEMM (1 GiB write outside the timed interval)", "parallelism": "replicas"}
+
+
+def main():
+    args = parse_args()
+    args.sizes_list = [int(x) for x in args.sizes.split(",")] if args.sizes else None
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from cs464_b200.keys import parse_key
+    from cs464_b200.matmul import B200Matmul, matmul
+    from cs464_b200.select import heuristic_config
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sizes = args.sizes_list or SIZES
+    g = torch.Generator(device=dev).manual_seed(0)
+    work = []
+    for n in sizes:
+        a = torch.randn((n, n), generator=g, device=dev, dtype=torch.float32).to(torch.float16)
+        b = torch.randn((n, n), generator=g, device=dev, dtype=torch.float32).to(torch.float16)
+        cfg = parse_key(args.config) if args.config else heuristic_config(n, n, n)
+        c = torch.empty((n, n), device=dev, dtype=torch.float16)
+        run = B200Matmul(cfg).make_runner(a, b, out=c)
+        work.append({"n": n, "a": a, "b": b, "c": c, "cfg": cfg, "run": run, "flops": 2.0 * n ** 3})
+    flush_buf = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def one_step(record: list | None):
+        for i, w in enumerate(work):
+            flush_buf.zero_()
+            if record is None:
+                w["run"]()
+            else:
+                s, e = record[i]
+                s.record(stream)
+                w["run"]()
+                e.record(stream)
+
+    for _ in range(args.warmup):
+        one_step(None)
+    torch.cuda.synchronize()
+    uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    sampler = ClockSampler(uuid)
+    events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in work]
+              for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    for k in range(args.steps):
+        one_step(events[k])
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    per_size_ms = [sum(events[k][i][0].elapsed_time(events[k][i][1]) for k in range(args.steps)) / args.steps
+                   for i in range(len(work))]
+    total_ms = sum(per_size_ms) * args.steps
+    total_ms_max = max_over_ranks(total_ms)
+    flops_step = sum(w["flops"] for w in work)
+    value = flops_step * args.steps * world / (total_ms_max / 1e3) / 1e12
+    for w in work:
+        w["run"].raise_on_status()
+    launches = sum(w["run"].num_kernels for w in work) * args.steps
+
+    peak, peak_src, _ = measured_peaks()
+    dom = max(range(len(work)), key=lambda i: per_size_ms[i])
+    achieved = work[dom]["flops"] / (per_size_ms[dom] / 1e3) / 1e12
+    traffic = TRAFFIC_BYTES_16384 if work[dom]["n"] == 16384 else None
+
+    # end to end through the public API: pinned host inputs copied in, matmul(), result copied back, every step
+    e2e = None
+    if not args.no_e2e:
+        host = []
+        for w in work:
+            ha = torch.empty_like(w["a"], device="cpu").pin_memory()
+            hb = torch.empty_like(w["b"], device="cpu").pin_memory()
+            hc = torch.empty_like(w["c"], device="cpu").pin_memory()
+            ha.copy_(w["a"])
+            hb.copy_(w["b"])
+            host.append((ha, hb, hc))
+        h2d = sum(ha.numel() * 2 + hb.numel() * 2 for ha, hb, _ in host)
+        d2h = sum(hc.numel() * 2 for _, _, hc in host)
+
+        def e2e_step():
+            for w, (ha, hb, hc) in zip(work, host):
+                a = ha.to(dev, non_blocking=True)
+                b = hb.to(dev, non_blocking=True)
+                c = matmul(a, b, w["cfg"])
+                hc.copy_(c, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2e_steps = max(1, min(args.steps, 5))
+        s.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(s.elapsed_time(e))
+        e2e = {"value": round(flops_step * e2e_steps * world / (e2e_ms / 1e3) / 1e12, 3), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": round(e2e_ms / e2e_steps, 3),
+               "api": "cs464_b200.matmul(a, b, cfg) on tensors copied from pinned host memory, result copied back"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tfl, sec, threads, sample = cpu_reference([n for n in sizes if n <= max(CPU_SAMPLE_SIZES)] or [256], 10, 3,
+                                                  budget_s=30.0)
+        cpu = {"value": round(tfl, 4), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total_ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": {**workload_config(args), "selection": {str(w["n"]): w["cfg"].key() for w in work}},
+        "pct_of_peak": round(100.0 * value / world / peak, 2),
+        "per_size": {str(w["n"]): {"tflops": round(w["flops"] / (per_size_ms[i] / 1e3) / 1e12, 2),
+                                   "ms": round(per_size_ms[i], 4)} for i, w in enumerate(work)},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": f"b2g::gemm_kernel at {work[dom]['n']}^3 ({work[dom]['cfg'].key()})",
+                     "peak_source": peak_src},
+        "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": launches, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

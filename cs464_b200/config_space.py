@@ -29,7 +29,9 @@ SPACE = {
 
 TMEM_COLUMNS = 512
 CTL_SMEM_BYTES = 2048          # barriers + alignment slack in front of the ring (kCtlBytes + kAlignSlack)
-MIN_RING_BYTES = 32 * 1024     # below this a CTA cannot keep enough loads in flight to cover HBM latency
+# Little's law: ~6.5 TB/s x ~1.5 us of load latency over 148 SMs is ~66 KB in flight per SM; a ring smaller than
+# 64 KB cannot cover it
+MIN_RING_BYTES = 64 * 1024
 
 
 @dataclass(frozen=True)

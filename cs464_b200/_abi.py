@@ -28,6 +28,7 @@ EXPORTS = (
     "b2g_abi_version", "b2g_version", "b2g_source_hash", "b2g_last_error", "b2g_error_string", "b2g_status_string",
     "b2g_check", "b2g_workspace_size", "b2g_smem_bytes", "b2g_plan_create", "b2g_plan_launch",
     "b2g_plan_num_kernels", "b2g_plan_grid", "b2g_plan_destroy", "b2g_gemm", "b2g_splitk_reduce",
+    "b2g_gemm_noalloc",
 )
 
 
@@ -84,6 +85,7 @@ def _declare(lib: ctypes.CDLL) -> None:
                                c_void_p]),
         "b2g_splitk_reduce": (c_int32, [c_void_p, c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                         ctypes.c_int64, c_int32, c_int32, c_void_p]),
+        "b2g_gemm_noalloc": (c_int32, [P(Config), P(Problem), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -744,6 +744,157 @@ int grid_for(int64_t work, int per_block) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(g, 148 * 16)));
 }
 
+// Fill `p` (caller-owned) with the launch plan of (cfg, prob) on the current device.
+int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, const void* A, const void* B, void* C,
+                  void* workspace, size_t workspace_bytes, int32_t* status) {
+  Geometry g;
+  int32_t rc = make_geometry(cfg, prob, g, A, B);
+  if (rc != B2G_OK) return rc;
+  const int64_t M = prob->M, N = prob->N, K = prob->K;
+  if ((M > 0 && N > 0) && (!C || (K > 0 && (!A || !B)))) return fail(B2G_ERR_INVALID_ARG, "null A, B or C");
+  if (g.ws_total > 0 && (workspace == nullptr || workspace_bytes < g.ws_total)) {
+    char buf[160];
+    snprintf(buf, sizeof buf, "workspace of %zu bytes needed, %zu given", g.ws_total,
+             workspace == nullptr ? size_t(0) : workspace_bytes);
+    return fail(B2G_ERR_WORKSPACE, buf);
+  }
+  if (g.ws_total > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(B2G_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return fail(B2G_ERR_CUDA, cudaGetErrorString(ce));
+  int sm_count = 0;
+  rc = init_device(dev, sm_count);
+  if (rc != B2G_OK) return rc;
+
+  memset(p, 0, sizeof(*p));
+  p->device = dev;
+  p->empty = (M == 0 || N == 0);
+  p->k_zero = (K == 0);
+  const int bf16 = prob->dtype == B2G_DTYPE_BF16;
+  if (!p->empty && p->k_zero) {
+    p->reduce = 1;
+    p->r_ws = nullptr;
+    p->r_c = C;
+    p->r_M = M;
+    p->r_N = N;
+    p->r_scm = prob->stride_cm;
+    p->r_scn = prob->stride_cn;
+    p->r_split = 0;
+    p->r_bf16 = bf16;
+    p->r_vec = 0;
+  }
+  if (!p->empty && !p->k_zero) {
+    const void* a_base = g.a.src;
+    const void* b_base = g.b.src;
+    if (g.a.pack) {
+      p->pack_a = 1;
+      fill_pack(g.a, workspace, p->pa_src, p->pa_so, p->pa_si, p->pa_ld, p->pa_outer, p->pa_inner, p->pa_dst);
+      a_base = p->pa_dst;
+    }
+    if (g.b.pack) {
+      p->pack_b = 1;
+      fill_pack(g.b, workspace, p->pb_src, p->pb_so, p->pb_si, p->pb_ld, p->pb_outer, p->pb_inner, p->pb_dst);
+      b_base = p->pb_dst;
+    }
+    rc = encode_operand(g.a, a_base, prob->dtype, g.bk, &p->tma_a);
+    if (rc == B2G_OK) rc = encode_operand(g.b, b_base, prob->dtype, g.bk, &p->tma_b);
+    if (rc != B2G_OK) return rc;
+    KParams& k = p->kp;
+    k.rows_a = static_cast<int32_t>(g.swapped ? N : M);
+    k.rows_b = static_cast<int32_t>(g.swapped ? M : N);
+    k.K = static_cast<int32_t>(K);
+    k.tile_m = g.tile_m;
+    k.tile_n = g.tile_n;
+    k.bk = g.bk;
+    k.stages = g.stages;
+    k.group_m = cfg->group_m;
+    k.split_k = cfg->split_k;
+    k.tiles_m = g.tiles_m;
+    k.tiles_n = g.tiles_n;
+    k.num_kb = g.num_kb;
+    k.units = g.units;
+    k.a_mn_major = g.a.mn_major;
+    k.b_mn_major = g.b.mn_major;
+    k.idesc = idesc_f16(bf16 ? 1u : 0u, static_cast<uint32_t>(g.a.mn_major), static_cast<uint32_t>(g.b.mn_major),
+                        128u, static_cast<uint32_t>(g.tile_n));
+    k.a_stage_bytes = static_cast<uint32_t>(g.tile_m * g.bk * 2);
+    k.b_stage_bytes = static_cast<uint32_t>(g.tile_n * g.bk * 2);
+    k.acc_cols = g.acc_cols;
+    k.num_acc = g.num_acc;
+    k.tmem_cols = g.tmem_cols;
+    k.status = status;
+    k.timeout_ns = kWaitTimeoutNs;
+    if (cfg->split_k > 1) {
+      k.out = workspace;
+      k.out_kind = OUT_F32_PARTIAL;
+      k.out_split_stride = M * N;
+      k.out_si = g.swapped ? 1 : N;
+      k.out_sj = g.swapped ? N : 1;
+      k.vec_ok = (k.out_sj == 1) && (k.out_si % 4 == 0);
+      p->reduce = 1;
+      p->r_ws = static_cast<const float*>(workspace);
+      p->r_c = C;
+      p->r_M = M;
+      p->r_N = N;
+      p->r_scm = prob->stride_cm;
+      p->r_scn = prob->stride_cn;
+      p->r_split = cfg->split_k;
+      p->r_bf16 = bf16;
+      p->r_vec = (N % 4 == 0) && prob->stride_cn == 1 && (prob->stride_cm % 4 == 0) &&
+                 ((reinterpret_cast<uintptr_t>(C) & 7u) == 0);
+    } else {
+      k.out = C;
+      k.out_kind = bf16 ? OUT_BF16 : OUT_F16;
+      k.out_split_stride = 0;
+      k.out_si = g.swapped ? prob->stride_cn : prob->stride_cm;
+      k.out_sj = g.swapped ? prob->stride_cm : prob->stride_cn;
+      k.vec_ok = (k.out_sj == 1) && (k.out_si % 8 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+    }
+    p->epi_warps = g.epi_warps;
+    p->threads = (2 + g.epi_warps) * 32;
+    p->smem = g.smem;
+    int64_t grid = g.units;
+    if (cfg->schedule == B2G_SCHED_PERSISTENT) {
+      int occ = 0;
+      ce = (g.epi_warps == 4)
+               ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_kernel<4>, p->threads, p->smem)
+               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_kernel<8>, p->threads, p->smem);
+      if (ce != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(ce));
+      occ = std::max(1, std::min<int>(occ, static_cast<int>(512 / g.tmem_cols)));
+      grid = std::min<int64_t>(grid, static_cast<int64_t>(sm_count) * occ);
+    }
+    p->grid = static_cast<int>(std::max<int64_t>(grid, 1));
+  }
+  return B2G_OK;
+}
+
+// ---------------------------------------------------------------- allocation-free entry point
+// Some callers may not allocate device memory at all (see b2g_gemm_noalloc in b2g.h). Their split-K partials live
+// in this fixed array instead of a caller workspace. It is part of the module image, so every GPU that loads this
+// library holds kNoAllocScratchBytes of it until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB: 8M fp32 partials
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct ScratchAddress {
+  std::once_flag flag;
+  cudaError_t err = cudaSuccess;
+  void* ptr = nullptr;
+};
+ScratchAddress g_scratch_address[64];
+
+// Device address of g_noalloc_scratch on `dev` (the current device). In host code the array's name is only a
+// host-side handle, so the address is looked up once per device and cached.
+int32_t noalloc_scratch(int dev, void*& ptr) {
+  if (dev < 0 || dev >= 64) return fail(B2G_ERR_CUDA, "device index out of range");
+  ScratchAddress& s = g_scratch_address[dev];
+  std::call_once(s.flag, [&s] { s.err = cudaGetSymbolAddress(&s.ptr, g_noalloc_scratch); });
+  if (s.err != cudaSuccess || s.ptr == nullptr)
+    return fail(B2G_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(s.err));
+  ptr = s.ptr;
+  return B2G_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -813,131 +964,11 @@ int32_t b2g_plan_create(const b2g_config* cfg, const b2g_problem* prob, const vo
                         void* workspace, size_t workspace_bytes, int32_t* status, b2g_plan** out) {
   if (!out) return fail(B2G_ERR_INVALID_ARG, "null plan output");
   *out = nullptr;
-  Geometry g;
-  int32_t rc = make_geometry(cfg, prob, g, A, B);
-  if (rc != B2G_OK) return rc;
-  const int64_t M = prob->M, N = prob->N, K = prob->K;
-  if ((M > 0 && N > 0) && (!C || (K > 0 && (!A || !B)))) return fail(B2G_ERR_INVALID_ARG, "null A, B or C");
-  if (g.ws_total > 0 && (workspace == nullptr || workspace_bytes < g.ws_total)) {
-    char buf[160];
-    snprintf(buf, sizeof buf, "workspace of %zu bytes needed, %zu given", g.ws_total,
-             workspace == nullptr ? size_t(0) : workspace_bytes);
-    return fail(B2G_ERR_WORKSPACE, buf);
-  }
-  if (g.ws_total > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
-    return fail(B2G_ERR_WORKSPACE, "workspace must be 256-byte aligned");
-  int dev = 0;
-  cudaError_t ce = cudaGetDevice(&dev);
-  if (ce != cudaSuccess) return fail(B2G_ERR_CUDA, cudaGetErrorString(ce));
-  int sm_count = 0;
-  rc = init_device(dev, sm_count);
-  if (rc != B2G_OK) return rc;
-
   b2g_plan* p = new b2g_plan();
-  memset(p, 0, sizeof(*p));
-  p->device = dev;
-  p->empty = (M == 0 || N == 0);
-  p->k_zero = (K == 0);
-  const int bf16 = prob->dtype == B2G_DTYPE_BF16;
-  if (!p->empty && p->k_zero) {
-    p->reduce = 1;
-    p->r_ws = nullptr;
-    p->r_c = C;
-    p->r_M = M;
-    p->r_N = N;
-    p->r_scm = prob->stride_cm;
-    p->r_scn = prob->stride_cn;
-    p->r_split = 0;
-    p->r_bf16 = bf16;
-    p->r_vec = 0;
-  }
-  if (!p->empty && !p->k_zero) {
-    const void* a_base = g.a.src;
-    const void* b_base = g.b.src;
-    if (g.a.pack) {
-      p->pack_a = 1;
-      fill_pack(g.a, workspace, p->pa_src, p->pa_so, p->pa_si, p->pa_ld, p->pa_outer, p->pa_inner, p->pa_dst);
-      a_base = p->pa_dst;
-    }
-    if (g.b.pack) {
-      p->pack_b = 1;
-      fill_pack(g.b, workspace, p->pb_src, p->pb_so, p->pb_si, p->pb_ld, p->pb_outer, p->pb_inner, p->pb_dst);
-      b_base = p->pb_dst;
-    }
-    rc = encode_operand(g.a, a_base, prob->dtype, g.bk, &p->tma_a);
-    if (rc == B2G_OK) rc = encode_operand(g.b, b_base, prob->dtype, g.bk, &p->tma_b);
-    if (rc != B2G_OK) {
-      delete p;
-      return rc;
-    }
-    KParams& k = p->kp;
-    k.rows_a = static_cast<int32_t>(g.swapped ? N : M);
-    k.rows_b = static_cast<int32_t>(g.swapped ? M : N);
-    k.K = static_cast<int32_t>(K);
-    k.tile_m = g.tile_m;
-    k.tile_n = g.tile_n;
-    k.bk = g.bk;
-    k.stages = g.stages;
-    k.group_m = cfg->group_m;
-    k.split_k = cfg->split_k;
-    k.tiles_m = g.tiles_m;
-    k.tiles_n = g.tiles_n;
-    k.num_kb = g.num_kb;
-    k.units = g.units;
-    k.a_mn_major = g.a.mn_major;
-    k.b_mn_major = g.b.mn_major;
-    k.idesc = idesc_f16(bf16 ? 1u : 0u, static_cast<uint32_t>(g.a.mn_major), static_cast<uint32_t>(g.b.mn_major),
-                        128u, static_cast<uint32_t>(g.tile_n));
-    k.a_stage_bytes = static_cast<uint32_t>(g.tile_m * g.bk * 2);
-    k.b_stage_bytes = static_cast<uint32_t>(g.tile_n * g.bk * 2);
-    k.acc_cols = g.acc_cols;
-    k.num_acc = g.num_acc;
-    k.tmem_cols = g.tmem_cols;
-    k.status = status;
-    k.timeout_ns = kWaitTimeoutNs;
-    if (cfg->split_k > 1) {
-      k.out = workspace;
-      k.out_kind = OUT_F32_PARTIAL;
-      k.out_split_stride = M * N;
-      k.out_si = g.swapped ? 1 : N;
-      k.out_sj = g.swapped ? N : 1;
-      k.vec_ok = (k.out_sj == 1) && (k.out_si % 4 == 0);
-      p->reduce = 1;
-      p->r_ws = static_cast<const float*>(workspace);
-      p->r_c = C;
-      p->r_M = M;
-      p->r_N = N;
-      p->r_scm = prob->stride_cm;
-      p->r_scn = prob->stride_cn;
-      p->r_split = cfg->split_k;
-      p->r_bf16 = bf16;
-      p->r_vec = (N % 4 == 0) && prob->stride_cn == 1 && (prob->stride_cm % 4 == 0) &&
-                 ((reinterpret_cast<uintptr_t>(C) & 7u) == 0);
-    } else {
-      k.out = C;
-      k.out_kind = bf16 ? OUT_BF16 : OUT_F16;
-      k.out_split_stride = 0;
-      k.out_si = g.swapped ? prob->stride_cn : prob->stride_cm;
-      k.out_sj = g.swapped ? prob->stride_cm : prob->stride_cn;
-      k.vec_ok = (k.out_sj == 1) && (k.out_si % 8 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
-    }
-    p->epi_warps = g.epi_warps;
-    p->threads = (2 + g.epi_warps) * 32;
-    p->smem = g.smem;
-    int64_t grid = g.units;
-    if (cfg->schedule == B2G_SCHED_PERSISTENT) {
-      int occ = 0;
-      ce = (g.epi_warps == 4)
-               ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_kernel<4>, p->threads, p->smem)
-               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_kernel<8>, p->threads, p->smem);
-      if (ce != cudaSuccess) {
-        delete p;
-        return fail(B2G_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(ce));
-      }
-      occ = std::max(1, std::min<int>(occ, static_cast<int>(512 / g.tmem_cols)));
-      grid = std::min<int64_t>(grid, static_cast<int64_t>(sm_count) * occ);
-    }
-    p->grid = static_cast<int>(std::max<int64_t>(grid, 1));
+  const int32_t rc = plan_init(p, cfg, prob, A, B, C, workspace, workspace_bytes, status);
+  if (rc != B2G_OK) {
+    delete p;
+    return rc;
   }
   *out = p;
   return B2G_OK;
@@ -1010,6 +1041,36 @@ int32_t b2g_splitk_reduce(const float* ws, void* C, int64_t M, int64_t N, int64_
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
   return B2G_OK;
+}
+
+int32_t b2g_gemm_noalloc(const b2g_config* cfg, const b2g_problem* prob, const void* A, const void* B, void* C,
+                         int32_t* status, void* stream) {
+  Geometry g;
+  int32_t rc = make_geometry(cfg, prob, g, A, B);
+  if (rc != B2G_OK) return rc;
+  if (g.a.pack || g.b.pack)
+    return fail(B2G_ERR_UNSUPPORTED,
+                "operand_needs_staging: the allocation-free entry point reads A and B in place; it needs 16-byte "
+                "aligned bases and leading dimensions that are multiples of 8 elements (or unit-stride transposes)");
+  if (g.ws_total > kNoAllocScratchBytes) {
+    char buf[200];
+    snprintf(buf, sizeof buf,
+             "split-K partials need %zu bytes; the allocation-free entry point's scratch holds %zu bytes (32 MiB): "
+             "lower SPLIT_K or use b2g_plan_create with a workspace",
+             g.ws_total, kNoAllocScratchBytes);
+    return fail(B2G_ERR_WORKSPACE, buf);
+  }
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return fail(B2G_ERR_CUDA, cudaGetErrorString(ce));
+  void* scratch = nullptr;
+  rc = noalloc_scratch(dev, scratch);
+  if (rc != B2G_OK) return rc;
+  // Nothing in the scratch needs clearing: each call's GEMM writes every partial element its reduce then reads.
+  b2g_plan plan;
+  rc = plan_init(&plan, cfg, prob, A, B, C, scratch, kNoAllocScratchBytes, status);
+  if (rc != B2G_OK) return rc;
+  return b2g_plan_launch(&plan, stream);
 }
 
 }  // extern "C"

@@ -127,6 +127,27 @@ int32_t b2g_gemm(const b2g_config* cfg, const b2g_problem* prob, const void* A, 
 int32_t b2g_splitk_reduce(const float* ws, void* C, int64_t M, int64_t N, int64_t stride_cm, int64_t stride_cn,
                           int32_t split, int32_t dtype, void* stream);
 
+/* Allocation-free GEMM. It has no counterpart in the reference: the reference always allocates its split-K workspace
+   with torch (kernels/triton_matmul.py:133).
+   For callers that may not allocate device memory themselves: plugin hosts that hand a library only its input and
+   output buffers, processes whose device memory is already fully reserved by another allocator, and code running
+   while a stream is being captured in global mode, where cudaMalloc is not permitted. This entry point allocates
+   nothing (no cudaMalloc, no cudaFree, no allocating library call). The caller passes A, B and C (and optionally a
+   device status word); split-K partials go to a fixed scratch array that lives in the library's module image, 32 MiB
+   on every GPU that loads the library, held until the process exits.
+   Limits and rules:
+   - split-K partials larger than 32 MiB (4 * SPLIT_K * M * N bytes) are rejected with B2G_ERR_WORKSPACE and a
+     message naming both sizes; operands that would need staging (unaligned bases or leading dimensions) are
+     rejected with B2G_ERR_UNSUPPORTED.
+   - The first call on each device looks up the scratch array's device address (cudaGetSymbolAddress) with that
+     device current; make that first call before any stream capture begins.
+   - All calls share the one scratch array, which keeps the contents of the last call. Nothing in it needs to start
+     at zero: every partial a call reads is written by the same call. Calls whose kernels overlap on the GPU (other
+     streams, other threads) race on the array: serialise them.
+   Returns B2G_OK after enqueueing the kernels on `stream`. */
+int32_t b2g_gemm_noalloc(const b2g_config* cfg, const b2g_problem* prob, const void* A, const void* B, void* C,
+                         int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

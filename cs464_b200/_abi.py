@@ -35,7 +35,8 @@ EXPORTS = (
 class Config(ctypes.Structure):
     _fields_ = [("block_m", ctypes.c_int32), ("block_n", ctypes.c_int32), ("block_k", ctypes.c_int32),
                 ("num_warps", ctypes.c_int32), ("num_stages", ctypes.c_int32), ("group_m", ctypes.c_int32),
-                ("split_k", ctypes.c_int32), ("schedule", ctypes.c_int32), ("reserved", ctypes.c_int32 * 8)]
+                ("split_k", ctypes.c_int32), ("schedule", ctypes.c_int32), ("cluster", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 7)]
 
 
 class Problem(ctypes.Structure):

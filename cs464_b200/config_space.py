@@ -25,6 +25,7 @@ SPACE = {
     "GROUP_M": [1, 4, 8, 16],
     "SPLIT_K": [1, 2, 4, 8, 16],
     "PERSISTENT": [1, 0],
+    "CLUSTER": [1, 2],                   # 2: CTA pair on two SMs, M = 256 tcgen05 MMAs
 }
 
 TMEM_COLUMNS = 512
@@ -63,19 +64,22 @@ def swapped(cfg: MatmulConfig) -> bool:
 
 
 def mma_tile(cfg: MatmulConfig) -> tuple[int, int]:
-    """(rows on the tensor core's M side, columns on its N side) of one CTA tile."""
+    """(rows on the tensor core's M side, columns on its N side) of one tile (of the pair, with CLUSTER=2)."""
     return (cfg.BLOCK_N, cfg.BLOCK_M) if swapped(cfg) else (cfg.BLOCK_M, cfg.BLOCK_N)
 
 
 def smem_bytes(cfg: MatmulConfig, elem_bytes: int = 2) -> int:
-    """Dynamic shared memory of one CTA: control block + num_stages x (A tile + B tile)."""
-    return CTL_SMEM_BYTES + cfg.num_stages * (cfg.BLOCK_M + cfg.BLOCK_N) * cfg.BLOCK_K * elem_bytes
+    """Dynamic shared memory of one CTA: control block + num_stages x (A tile + B tile); a pair's CTA holds halves."""
+    rows = cfg.BLOCK_M + cfg.BLOCK_N
+    if cfg.CLUSTER == 2:
+        rows //= 2
+    return CTL_SMEM_BYTES + cfg.num_stages * rows * cfg.BLOCK_K * elem_bytes
 
 
 def tmem_columns(cfg: MatmulConfig) -> int:
-    """fp32 accumulator columns of one tile (one column per output column per 128 rows)."""
+    """fp32 accumulator columns of one CTA (one column per output column per 128 rows it owns)."""
     tm, tn = mma_tile(cfg)
-    return tm // 128 * tn
+    return tn if cfg.CLUSTER == 2 else tm // 128 * tn
 
 
 def static_violations(cfg: MatmulConfig, hw: HwLimits, elem_bytes: int = 2) -> list[str]:
@@ -90,12 +94,15 @@ def static_violations(cfg: MatmulConfig, hw: HwLimits, elem_bytes: int = 2) -> l
     elif cfg.BLOCK_N % 64:
         # B (N-contiguous) is read in 64-column, 128-byte swizzle atoms
         reasons.append("block_n_not_multiple_of_64")
+    if cfg.CLUSTER == 2 and tm != 256:
+        # the pair splits a 256-row tensor-core tile into two 128-row halves
+        reasons.append("cluster_needs_256_rows")
     if tmem_columns(cfg) > hw.tmem_columns:
         reasons.append("tmem_exceeds_limit")
     if cfg.num_warps == 8 and tn <= 32:
         # a second epilogue warpgroup would have no 32-column chunk of its own
         reasons.append("epilogue_warps_idle")
-    if cfg.num_stages * (cfg.BLOCK_M + cfg.BLOCK_N) * cfg.BLOCK_K * elem_bytes < MIN_RING_BYTES:
+    if smem_bytes(cfg, elem_bytes) - CTL_SMEM_BYTES < MIN_RING_BYTES:
         reasons.append("ring_too_shallow")
     return reasons
 
@@ -141,7 +148,7 @@ def prune(configs: list[MatmulConfig], hw: HwLimits, shape: tuple[int, int, int]
 
 # Hand-picked starting configs, one per regime (the reference's HANDPICKED, kernels/config_space.py:109-115).
 HANDPICKED = {
-    "large_square": MatmulConfig(128, 256, 64, num_warps=4, num_stages=4, GROUP_M=8),
+    "large_square": MatmulConfig(256, 256, 64, num_warps=4, num_stages=6, GROUP_M=8, CLUSTER=2),
     "medium": MatmulConfig(128, 128, 64, num_warps=4, num_stages=6, GROUP_M=8),
     "small_tile": MatmulConfig(128, 64, 64, num_warps=4, num_stages=8, GROUP_M=8),
     "skinny_m": MatmulConfig(16, 128, 128, num_warps=4, num_stages=6, GROUP_M=1),

@@ -66,6 +66,7 @@ enum OutKind : int32_t { OUT_F16 = 0, OUT_BF16 = 1, OUT_F32_PARTIAL = 2 };
 struct KParams {
   int32_t rows_a, rows_b, K;
   int32_t tile_m, tile_n, bk, stages;
+  int32_t cta_m, cta_n;  // A and B rows one CTA loads (tile_m, tile_n; halves of them in a CTA pair)
   int32_t group_m, split_k;
   int32_t tiles_m, tiles_n, num_kb, units;
   int32_t a_mn_major, b_mn_major;
@@ -193,7 +194,8 @@ __device__ __forceinline__ void store_chunk(const KParams& p, int split, int64_t
   }
 }
 
-template <int EPI_WARPS>
+// One CTA (PAIR = 0) or one CTA of a pair (PAIR = 1, cluster of 2, cta_group::2 MMAs of M = 256).
+template <int EPI_WARPS, int PAIR>
 __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     gemm_kernel(const __grid_constant__ KParams p, const __grid_constant__ CUtensorMap tma_a,
                 const __grid_constant__ CUtensorMap tma_b) {
@@ -204,6 +206,10 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t stage_bytes = p.a_stage_bytes + p.b_stage_bytes;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int first_unit = PAIR ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int unit_step = PAIR ? static_cast<int>(num_clusters_x()) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -212,7 +218,7 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(ctl + OFF_TFULL + 8 * b, 1);
-      mbar_init(ctl + OFF_TEMPTY + 8 * b, EPI_WARPS * 32);
+      mbar_init(ctl + OFF_TEMPTY + 8 * b, (PAIR ? 2 : 1) * EPI_WARPS * 32);
     }
     mbar_init(ctl + OFF_DRAIN, 1);
     *abort_flag = 0u;
@@ -221,25 +227,35 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     tma_prefetch_desc(&tma_b);
   }
   if (warp == 1) {
-    tmem_alloc(ctl + OFF_TMEM, p.tmem_cols);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(ctl + OFF_TMEM, p.tmem_cols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(ctl + OFF_TMEM, p.tmem_cols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) {
+    cluster_sync();  // both CTAs' barriers initialised and tensor memory allocated before any cross-CTA signal
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(smem_raw + OFF_TMEM);
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer (every CTA loads its own tiles)
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
       int issued = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+      const uint32_t tx_bytes = PAIR ? 2u * stage_bytes : stage_bytes;
+      for (int u = first_unit; u < p.units && ok; u += unit_step) {
         const Unit w = decode_unit(p, u);
-        const int row_a = w.tm * p.tile_m;
-        const int row_b = w.tn * p.tile_n;
+        const int row_a = w.tm * p.tile_m + static_cast<int>(rank) * p.cta_m;
+        const int row_b = w.tn * p.tile_n + static_cast<int>(rank) * p.cta_n;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!wait_phase(ctl + OFF_EMPTY + 8 * s, ph ^ 1u, abort_flag, p.status, p.timeout_ns,
                           kStatusProducerTimeout)) {
@@ -247,21 +263,33 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
             break;
           }
           const uint32_t full = ctl + OFF_FULL + 8 * s;
-          mbar_arrive_expect_tx(full, stage_bytes);
+          // the pair's leader counts both CTAs' bytes on its own barrier; the peer only issues copies
+          if (leader) mbar_arrive_expect_tx(full, tx_bytes);
+          const uint32_t full_c = PAIR ? map_to_rank(full, 0) : full;
           const uint32_t sa = data + s * stage_bytes;
           const uint32_t sb = sa + p.a_stage_bytes;
           const int k0 = kb * p.bk;
           if (p.a_mn_major) {
-            for (int a = 0; a < p.tile_m / 64; ++a)
-              tma_load_2d(sa + a * p.bk * 128, &tma_a, full, row_a + a * 64, k0);
+            for (int a = 0; a < p.cta_m / 64; ++a) {
+              if (PAIR) tma_load_2d_pair(sa + a * p.bk * 128, &tma_a, full_c, row_a + a * 64, k0);
+              else tma_load_2d(sa + a * p.bk * 128, &tma_a, full, row_a + a * 64, k0);
+            }
           } else {
-            for (int a = 0; a < p.bk / 64; ++a) tma_load_2d(sa + a * p.tile_m * 128, &tma_a, full, k0 + a * 64, row_a);
+            for (int a = 0; a < p.bk / 64; ++a) {
+              if (PAIR) tma_load_2d_pair(sa + a * p.cta_m * 128, &tma_a, full_c, k0 + a * 64, row_a);
+              else tma_load_2d(sa + a * p.cta_m * 128, &tma_a, full, k0 + a * 64, row_a);
+            }
           }
           if (p.b_mn_major) {
-            for (int a = 0; a < p.tile_n / 64; ++a)
-              tma_load_2d(sb + a * p.bk * 128, &tma_b, full, row_b + a * 64, k0);
+            for (int a = 0; a < p.cta_n / 64; ++a) {
+              if (PAIR) tma_load_2d_pair(sb + a * p.bk * 128, &tma_b, full_c, row_b + a * 64, k0);
+              else tma_load_2d(sb + a * p.bk * 128, &tma_b, full, row_b + a * 64, k0);
+            }
           } else {
-            for (int a = 0; a < p.bk / 64; ++a) tma_load_2d(sb + a * p.tile_n * 128, &tma_b, full, k0 + a * 64, row_b);
+            for (int a = 0; a < p.bk / 64; ++a) {
+              if (PAIR) tma_load_2d_pair(sb + a * p.cta_n * 128, &tma_b, full_c, k0 + a * 64, row_b);
+              else tma_load_2d(sb + a * p.cta_n * 128, &tma_b, full, k0 + a * 64, row_b);
+            }
           }
           ++issued;
           if (++s == p.stages) {
@@ -270,8 +298,9 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
           }
         }
       }
-      if (!ok) {
-        // Let the copies already issued land before the CTA's shared memory is released.
+      if (!ok && leader) {
+        // Let the copies already issued land before shared memory is released (the leader's barriers count the
+        // pair's bytes).
         const int pending = min(issued, p.stages);
         int ds = s;
         uint32_t dph = ph;
@@ -285,19 +314,19 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (the pair's leader issues for both)
+    if (lane == 0 && leader) {
       int s = 0;
       uint32_t ph = 0;
       uint32_t acc = 0, acc_ph = 0;
       bool ok = true;
-      const uint32_t k_atom_a = p.a_mn_major ? 0u : static_cast<uint32_t>(p.tile_m) * 128u;
-      const uint32_t k_atom_b = p.b_mn_major ? 0u : static_cast<uint32_t>(p.tile_n) * 128u;
+      const uint32_t k_atom_a = p.a_mn_major ? 0u : static_cast<uint32_t>(p.cta_m) * 128u;
+      const uint32_t k_atom_b = p.b_mn_major ? 0u : static_cast<uint32_t>(p.cta_n) * 128u;
       const uint32_t lbo_a = p.a_mn_major ? static_cast<uint32_t>(p.bk) * 128u : 16u;
       const uint32_t lbo_b = p.b_mn_major ? static_cast<uint32_t>(p.bk) * 128u : 16u;
       const int ksteps = p.bk / 16;
-      const int halves = p.tile_m / 128;
-      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+      const int halves = PAIR ? 1 : p.tile_m / 128;
+      for (int u = first_unit; u < p.units && ok; u += unit_step) {
         const Unit w = decode_unit(p, u);
         if (w.kb0 == w.kb1) continue;
         if (!wait_phase(ctl + OFF_TEMPTY + 8 * acc, acc_ph ^ 1u, abort_flag, p.status, p.timeout_ns,
@@ -321,39 +350,55 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
             const uint32_t b_k = p.b_mn_major ? kk * 2048u : (kk >> 2) * k_atom_b + (kk & 3) * 32u;
             const uint64_t bdesc = sdesc_sw128(sb + b_k, lbo_b, 1024u);
             for (int h = 0; h < halves; ++h) {
-              // rows 128h.. of the A tile: two 64-row atoms on for MN-major, 128 swizzled rows on for K-major
+              // rows 128h.. of a 256-row A tile: two 64-row atoms on for MN-major, 128 swizzled rows on for K-major
               const uint32_t a_h = p.a_mn_major ? h * 2u * static_cast<uint32_t>(p.bk) * 128u : h * 128u * 128u;
               const uint64_t adesc = sdesc_sw128(sa + a_h + a_k, lbo_a, 1024u);
-              umma_f16(d_base + h * p.tile_n, adesc, bdesc, p.idesc, (kb > w.kb0 || kk > 0) ? 1u : 0u);
+              const uint32_t accumulate = (kb > w.kb0 || kk > 0) ? 1u : 0u;
+              if (PAIR) umma_f16_pair(d_base, adesc, bdesc, p.idesc, accumulate);
+              else umma_f16(d_base + h * p.tile_n, adesc, bdesc, p.idesc, accumulate);
             }
           }
-          umma_commit(ctl + OFF_EMPTY + 8 * s);
+          if (PAIR) {
+            const uint32_t e = ctl + OFF_EMPTY + 8 * s;
+            umma_commit_pair(map_to_rank(e, 0));
+            umma_commit_pair(map_to_rank(e, 1));
+          } else {
+            umma_commit(ctl + OFF_EMPTY + 8 * s);
+          }
           if (++s == p.stages) {
             s = 0;
             ph ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(ctl + OFF_TFULL + 8 * acc);
+        if (PAIR) {
+          const uint32_t f = ctl + OFF_TFULL + 8 * acc;
+          umma_commit_pair(map_to_rank(f, 0));
+          umma_commit_pair(map_to_rank(f, 1));
+        } else {
+          umma_commit(ctl + OFF_TFULL + 8 * acc);
+        }
         if (++acc == p.num_acc) {
           acc = 0;
           acc_ph ^= 1u;
         }
       }
       // Every MMA this thread issued has finished before tensor memory is released.
-      umma_commit(ctl + OFF_DRAIN);
+      if (PAIR) umma_commit_pair(map_to_rank(ctl + OFF_DRAIN, 0));
+      else umma_commit(ctl + OFF_DRAIN);
       drain_phase(ctl + OFF_DRAIN, 0, ok ? kWaitTimeoutNs : kDrainTimeoutNs);
     }
   } else {
-    // ------------------------------------------------------------ epilogue
+    // ------------------------------------------------------------ epilogue (each CTA drains its own accumulator)
     const int e = warp - 2;
     const int q = warp & 3;  // tensor-memory lane quarter this warp may access
     const int grp = e >> 2;
     constexpr int kGroups = EPI_WARPS / 4;
     const int nchunks = (p.tile_n + 31) / 32;
-    const int halves = p.tile_m / 128;
+    const int halves = PAIR ? 1 : p.tile_m / 128;
+    const uint32_t tempty_leader = PAIR ? map_to_rank(ctl + OFF_TEMPTY, 0) : 0u;
     uint32_t acc = 0, acc_ph = 0;
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+    for (int u = first_unit; u < p.units; u += unit_step) {
       const Unit w = decode_unit(p, u);
       const bool zero = w.kb0 == w.kb1;
       if (!zero) {
@@ -363,7 +408,8 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
         tc_fence_after();
       }
       for (int h = 0; h < halves; ++h) {
-        const int64_t row = static_cast<int64_t>(w.tm) * p.tile_m + h * 128 + q * 32 + lane;
+        const int64_t row =
+            static_cast<int64_t>(w.tm) * p.tile_m + static_cast<int64_t>(rank) * p.cta_m + h * 128 + q * 32 + lane;
         for (int c = grp; c < nchunks; c += kGroups) {
           const int ncol = min(32, p.tile_n - c * 32);
           uint32_t v[32];
@@ -385,7 +431,8 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
       }
       if (!zero) {
         tc_fence_before();
-        mbar_arrive(ctl + OFF_TEMPTY + 8 * acc);
+        if (PAIR) mbar_arrive_cluster(tempty_leader + 8 * acc);
+        else mbar_arrive(ctl + OFF_TEMPTY + 8 * acc);
         if (++acc == p.num_acc) {
           acc = 0;
           acc_ph ^= 1u;
@@ -396,10 +443,15 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
 
   __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) {
+    cluster_sync();  // no CTA leaves while its peer may still signal it or read its shared memory
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, p.tmem_cols);
+    if (PAIR) tmem_dealloc_pair(tmem_base, p.tmem_cols);
+    else tmem_dealloc(tmem_base, p.tmem_cols);
   }
 }
 
@@ -547,7 +599,9 @@ size_t packed_bytes(const Operand& o) {
 
 struct Geometry {
   bool swapped;
+  int pair;
   int tile_m, tile_n, bk, stages, epi_warps;
+  int cta_m, cta_n;
   int tiles_m, tiles_n, num_kb, units;
   uint32_t acc_cols, num_acc, tmem_cols;
   size_t smem;
@@ -570,21 +624,32 @@ int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g,
   if (pr->M >= (int64_t(1) << 31) || pr->N >= (int64_t(1) << 31) || pr->K >= (int64_t(1) << 31))
     return fail(B2G_ERR_UNSUPPORTED, "dimension_too_large: each of M, N, K must be < 2^31");
   const int bm = cfg->block_m, bn = cfg->block_n, bk = cfg->block_k;
+  if (cfg->cluster != 0 && cfg->cluster != 1 && cfg->cluster != 2)
+    return fail(B2G_ERR_UNSUPPORTED, "cluster_invalid: cluster must be 1 or 2");
+  g.pair = cfg->cluster == 2;
   g.swapped = bm <= 64;
   if (g.swapped) {
     if (bm != 16 && bm != 32 && bm != 48 && bm != 64)
       return fail(B2G_ERR_UNSUPPORTED, "block_m_invalid: skinny BLOCK_M must be 16, 32, 48 or 64");
     if (bn != 128 && bn != 256)
       return fail(B2G_ERR_UNSUPPORTED, "block_n_invalid: BLOCK_M <= 64 needs BLOCK_N 128 or 256");
+    if (g.pair && bn != 256)
+      return fail(B2G_ERR_UNSUPPORTED, "cluster_tile_invalid: a CTA pair in the skinny form needs BLOCK_N 256");
     g.tile_m = bn;
     g.tile_n = bm;
   } else {
     if (bm != 128 && bm != 256) return fail(B2G_ERR_UNSUPPORTED, "block_m_invalid: BLOCK_M must be <= 64, 128 or 256");
     if (bn < 16 || bn > 256 || bn % 16 != 0)
       return fail(B2G_ERR_UNSUPPORTED, "block_n_invalid: BLOCK_N must be a multiple of 16 in [16, 256]");
+    if (g.pair && bm != 256)
+      return fail(B2G_ERR_UNSUPPORTED, "cluster_tile_invalid: a CTA pair needs BLOCK_M 256");
     g.tile_m = bm;
     g.tile_n = bn;
   }
+  if (g.pair && (g.tile_n % 16 != 0 || (g.tile_n / 2) % 8 != 0))
+    return fail(B2G_ERR_UNSUPPORTED, "cluster_tile_invalid: each CTA of a pair needs a multiple of 8 B rows");
+  g.cta_m = g.pair ? g.tile_m / 2 : g.tile_m;
+  g.cta_n = g.pair ? g.tile_n / 2 : g.tile_n;
   if (bk != 64 && bk != 128) return fail(B2G_ERR_UNSUPPORTED, "block_k_invalid: BLOCK_K must be 64 or 128");
   if (cfg->num_warps != 4 && cfg->num_warps != 8)
     return fail(B2G_ERR_UNSUPPORTED, "num_warps_invalid: epilogue warps must be 4 or 8");
@@ -602,11 +667,11 @@ int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g,
   // operands in MMA orientation
   Operand oa{}, ob{};
   if (!g.swapped) {
-    oa = Operand{A, M, K, pr->stride_am, pr->stride_ak, g.tile_m, 0, 0, 0, 0};
-    ob = Operand{B, N, K, pr->stride_bn, pr->stride_bk, g.tile_n, 0, 0, 0, 0};
+    oa = Operand{A, M, K, pr->stride_am, pr->stride_ak, g.cta_m, 0, 0, 0, 0};
+    ob = Operand{B, N, K, pr->stride_bn, pr->stride_bk, g.cta_n, 0, 0, 0, 0};
   } else {
-    oa = Operand{B, N, K, pr->stride_bn, pr->stride_bk, g.tile_m, 0, 0, 0, 0};
-    ob = Operand{A, M, K, pr->stride_am, pr->stride_ak, g.tile_n, 0, 0, 0, 0};
+    oa = Operand{B, N, K, pr->stride_bn, pr->stride_bk, g.cta_m, 0, 0, 0, 0};
+    ob = Operand{A, M, K, pr->stride_am, pr->stride_ak, g.cta_n, 0, 0, 0, 0};
   }
   layout_operand(oa);
   layout_operand(ob);
@@ -620,10 +685,11 @@ int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g,
   const int64_t units = static_cast<int64_t>(g.tiles_m) * g.tiles_n * cfg->split_k;
   if (units >= (int64_t(1) << 31)) return fail(B2G_ERR_UNSUPPORTED, "too_many_tiles");
   g.units = static_cast<int>(units);
-  g.acc_cols = static_cast<uint32_t>(g.tile_m / 128 * g.tile_n);
+  // fp32 accumulator columns per CTA: a pair's CTA holds its 128 rows x tile_n
+  g.acc_cols = static_cast<uint32_t>(g.pair ? g.tile_n : g.tile_m / 128 * g.tile_n);
   g.num_acc = (2 * g.acc_cols <= 512) ? 2u : 1u;
   g.tmem_cols = pow2_at_least(g.num_acc * g.acc_cols);
-  const size_t stage = static_cast<size_t>(g.tile_m + g.tile_n) * bk * 2;
+  const size_t stage = static_cast<size_t>(g.cta_m + g.cta_n) * bk * 2;
   g.smem = kCtlBytes + kAlignSlack + stage * g.stages;
   if (g.smem > kMaxSmemPerCta) return fail(B2G_ERR_UNSUPPORTED, "smem_exceeds_limit");
   const int64_t ws_elems = static_cast<int64_t>(cfg->split_k) * M * N;
@@ -647,11 +713,12 @@ int32_t init_device(int dev, int& sm_count) {
   if (dev < 0 || dev >= 64) return fail(B2G_ERR_CUDA, "device index out of range");
   DeviceInit& d = g_dev[dev];
   std::call_once(d.flag, [&d, dev] {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kMaxSmemPerCta));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemm_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(kMaxSmemPerCta));
+    const int smem = static_cast<int>(kMaxSmemPerCta);
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<4, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_kernel<8, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_kernel<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_kernel<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    // a pair is a 2-CTA cluster: always within the portable size, no opt-in needed
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
     d.err = e;
   });
@@ -701,6 +768,7 @@ struct b2g_plan {
   KParams kp;
   CUtensorMap tma_a, tma_b;
   int epi_warps;
+  int pair;
   int grid, threads;
   size_t smem;
   // packing
@@ -806,6 +874,8 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
     k.K = static_cast<int32_t>(K);
     k.tile_m = g.tile_m;
     k.tile_n = g.tile_n;
+    k.cta_m = g.cta_m;
+    k.cta_n = g.cta_n;
     k.bk = g.bk;
     k.stages = g.stages;
     k.group_m = cfg->group_m;
@@ -817,9 +887,9 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
     k.a_mn_major = g.a.mn_major;
     k.b_mn_major = g.b.mn_major;
     k.idesc = idesc_f16(bf16 ? 1u : 0u, static_cast<uint32_t>(g.a.mn_major), static_cast<uint32_t>(g.b.mn_major),
-                        128u, static_cast<uint32_t>(g.tile_n));
-    k.a_stage_bytes = static_cast<uint32_t>(g.tile_m * g.bk * 2);
-    k.b_stage_bytes = static_cast<uint32_t>(g.tile_n * g.bk * 2);
+                        g.pair ? 256u : 128u, static_cast<uint32_t>(g.tile_n));
+    k.a_stage_bytes = static_cast<uint32_t>(g.cta_m * g.bk * 2);
+    k.b_stage_bytes = static_cast<uint32_t>(g.cta_n * g.bk * 2);
     k.acc_cols = g.acc_cols;
     k.num_acc = g.num_acc;
     k.tmem_cols = g.tmem_cols;
@@ -852,17 +922,40 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
       k.vec_ok = (k.out_sj == 1) && (k.out_si % 8 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
     }
     p->epi_warps = g.epi_warps;
+    p->pair = g.pair;
     p->threads = (2 + g.epi_warps) * 32;
     p->smem = g.smem;
+    // grid in work units (CTAs, or CTA pairs)
     int64_t grid = g.units;
     if (cfg->schedule == B2G_SCHED_PERSISTENT) {
-      int occ = 0;
-      ce = (g.epi_warps == 4)
-               ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_kernel<4>, p->threads, p->smem)
-               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_kernel<8>, p->threads, p->smem);
-      if (ce != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(ce));
-      occ = std::max(1, std::min<int>(occ, static_cast<int>(512 / g.tmem_cols)));
-      grid = std::min<int64_t>(grid, static_cast<int64_t>(sm_count) * occ);
+      int64_t slots = 0;
+      if (g.pair) {
+        cudaLaunchConfig_t lc = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        lc.gridDim = dim3(2 * sm_count, 1, 1);
+        lc.blockDim = dim3(p->threads, 1, 1);
+        lc.dynamicSmemBytes = p->smem;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+        int nclusters = 0;
+        ce = (g.epi_warps == 4) ? cudaOccupancyMaxActiveClusters(&nclusters, gemm_kernel<4, 1>, &lc)
+                                : cudaOccupancyMaxActiveClusters(&nclusters, gemm_kernel<8, 1>, &lc);
+        if (ce != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("cluster occupancy query: ") + cudaGetErrorString(ce));
+        slots = std::max(1, nclusters);
+      } else {
+        int occ = 0;
+        ce = (g.epi_warps == 4)
+                 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_kernel<4, 0>, p->threads, p->smem)
+                 : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_kernel<8, 0>, p->threads, p->smem);
+        if (ce != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(ce));
+        occ = std::max(1, std::min<int>(occ, static_cast<int>(512 / g.tmem_cols)));
+        slots = static_cast<int64_t>(sm_count) * occ;
+      }
+      grid = std::min<int64_t>(grid, slots);
     }
     p->grid = static_cast<int>(std::max<int64_t>(grid, 1));
   }
@@ -951,11 +1044,11 @@ int32_t b2g_workspace_size(const b2g_config* cfg, const b2g_problem* prob, const
 
 int32_t b2g_smem_bytes(const b2g_config* cfg, const b2g_problem* prob, size_t* bytes) {
   if (!bytes) return fail(B2G_ERR_INVALID_ARG, "null bytes");
-  Geometry g;
-  int32_t rc = make_geometry(cfg, prob, g, reinterpret_cast<const void*>(256), reinterpret_cast<const void*>(256));
-  if (rc != B2G_OK && rc != B2G_ERR_UNSUPPORTED) return rc;
-  const size_t stage = static_cast<size_t>((cfg->block_m <= 64 ? cfg->block_n + cfg->block_m : cfg->block_m + cfg->block_n)) *
-                       cfg->block_k * 2;
+  if (!cfg) return fail(B2G_ERR_INVALID_ARG, "null config");
+  const bool pair = cfg->cluster == 2;
+  const int rows = cfg->block_m + cfg->block_n;  // A rows + B rows of one tile
+  const size_t stage = static_cast<size_t>(pair ? rows / 2 : rows) * cfg->block_k * 2;
+  (void)prob;
   *bytes = kCtlBytes + kAlignSlack + stage * cfg->num_stages;
   return B2G_OK;
 }
@@ -989,10 +1082,26 @@ int32_t b2g_plan_launch(const b2g_plan* p, void* stream) {
         p->pb_outer, p->pb_inner);
   }
   if (!p->k_zero) {
-    if (p->epi_warps == 4) {
-      gemm_kernel<4><<<p->grid, p->threads, p->smem, st>>>(p->kp, p->tma_a, p->tma_b);
+    if (p->pair) {
+      cudaLaunchConfig_t lc = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      lc.gridDim = dim3(2 * p->grid, 1, 1);
+      lc.blockDim = dim3(p->threads, 1, 1);
+      lc.dynamicSmemBytes = p->smem;
+      lc.stream = st;
+      lc.attrs = attr;
+      lc.numAttrs = 1;
+      cudaError_t le = (p->epi_warps == 4) ? cudaLaunchKernelEx(&lc, gemm_kernel<4, 1>, p->kp, p->tma_a, p->tma_b)
+                                           : cudaLaunchKernelEx(&lc, gemm_kernel<8, 1>, p->kp, p->tma_a, p->tma_b);
+      if (le != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("cluster launch: ") + cudaGetErrorString(le));
+    } else if (p->epi_warps == 4) {
+      gemm_kernel<4, 0><<<p->grid, p->threads, p->smem, st>>>(p->kp, p->tma_a, p->tma_b);
     } else {
-      gemm_kernel<8><<<p->grid, p->threads, p->smem, st>>>(p->kp, p->tma_a, p->tma_b);
+      gemm_kernel<8, 0><<<p->grid, p->threads, p->smem, st>>>(p->kp, p->tma_a, p->tma_b);
     }
   }
   if (p->reduce) {

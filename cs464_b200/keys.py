@@ -1,8 +1,8 @@
 """Config-key codec: `parse_key` inverts `MatmulConfig.key()` (the reference's tune/sweep.py:355-364).
 
 Keys of the reference's format (`bm128_bn256_bk32_w8_s3_g8_sk1`, 7 fields) parse unchanged; extension knobs follow
-as `_<letter><int>` suffixes (`_p0`: PERSISTENT=0) and are present only when they differ from their defaults, so a
-key with no suffix means the same 7 fields it always did.
+as `_<letter><int>` suffixes (`_p0`: PERSISTENT=0, `_c2`: CLUSTER=2) and are present only when they differ from
+their defaults, so a key with no suffix means the same 7 fields it always did.
 """
 from __future__ import annotations
 

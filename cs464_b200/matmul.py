@@ -2,7 +2,8 @@
 
 Mirrors kernels/triton_matmul.py (the reference's hot path) so its callers drive this family unchanged:
   * `MatmulConfig` keeps the seven tunables and their meaning (kernels/triton_matmul.py:20-35) and `key()` keeps the
-    reference's format; one extra knob (PERSISTENT) is appended to the key only when it differs from its default.
+    reference's format; extra knobs (PERSISTENT, CLUSTER) are appended to the key only when they differ from their
+    defaults.
   * `B200Matmul(cfg).make_runner(a, b, out=None)` allocates the output, split-K workspace and launch plan once and
     returns a zero-allocation closure that enqueues on the current stream (kernels/triton_matmul.py:103-147), so
     `tune/timing.py:benchmark` can capture it in a CUDA graph.
@@ -26,7 +27,7 @@ from cs464_b200 import _abi
 _DTYPES = {torch.float16: _abi.DTYPE_F16, torch.bfloat16: _abi.DTYPE_BF16}
 
 # extension knobs: key suffix letter -> (field, default)
-EXTENSIONS = {"p": ("PERSISTENT", 1)}
+EXTENSIONS = {"p": ("PERSISTENT", 1), "c": ("CLUSTER", 1)}
 
 
 @dataclass(frozen=True)
@@ -34,7 +35,9 @@ class MatmulConfig:
     """One kernel variant. BLOCK_M x BLOCK_N output tile, BLOCK_K K step, num_warps epilogue warps (4 or 8),
     num_stages shared-memory ring depth, GROUP_M L2 tile grouping, SPLIT_K deterministic K splits. BLOCK_M <= 64 runs
     the operand-swapped skinny form. PERSISTENT=1: one CTA per SM slot walks the tiles; 0: one CTA per (tile, split),
-    the reference's grid (kernels/triton_matmul.py:99-100)."""
+    the reference's grid (kernels/triton_matmul.py:99-100). CLUSTER=2: a pair of CTAs on two SMs computes each tile
+    with M=256 tcgen05 MMAs (BLOCK_M = 256, or BLOCK_N = 256 in the skinny form), each CTA loading half of A and half
+    of B."""
     BLOCK_M: int
     BLOCK_N: int
     BLOCK_K: int
@@ -43,6 +46,7 @@ class MatmulConfig:
     GROUP_M: int = 8
     SPLIT_K: int = 1
     PERSISTENT: int = 1
+    CLUSTER: int = 1
 
     def key(self) -> str:
         k = (f"bm{self.BLOCK_M}_bn{self.BLOCK_N}_bk{self.BLOCK_K}_w{self.num_warps}_s{self.num_stages}"
@@ -66,6 +70,7 @@ class MatmulConfig:
         c.block_m, c.block_n, c.block_k = self.BLOCK_M, self.BLOCK_N, self.BLOCK_K
         c.num_warps, c.num_stages, c.group_m, c.split_k = self.num_warps, self.num_stages, self.GROUP_M, self.SPLIT_K
         c.schedule = _abi.SCHED_PERSISTENT if self.PERSISTENT else _abi.SCHED_TILE
+        c.cluster = self.CLUSTER
         return c
 
 

@@ -49,6 +49,8 @@ extern "C" {
  * num_warps is the number of epilogue warps (4 or 8); num_stages the depth of the shared-memory ring.
  * BLOCK_M <= 64 selects the swapped-operand (skinny M) form: the tensor-core M side covers BLOCK_N columns of C and
  * the N side covers BLOCK_M rows of C.
+ * cluster = 2 computes each tile with a CTA pair on two SMs (cta_group::2 MMAs of M = 256): BLOCK_M = 256 (or, in the
+ * skinny form, BLOCK_N = 256) is split into two 128-row halves, each CTA loading its half of A and half of B.
  */
 typedef struct b2g_config {
   int32_t block_m;
@@ -59,7 +61,8 @@ typedef struct b2g_config {
   int32_t group_m;
   int32_t split_k;
   int32_t schedule; /* B2G_SCHED_* */
-  int32_t reserved[8];
+  int32_t cluster;  /* 1: one CTA per tile; 2: a CTA pair per tile */
+  int32_t reserved[7];
 } b2g_config;
 
 /*

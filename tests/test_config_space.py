@@ -26,7 +26,7 @@ def test_reference_keys_parse_unchanged():
     for r in RULES["shape_rules"][::13]:
         cfg = parse_key(r["key"])
         assert cfg.key() == r["key"]
-        assert {k: v for k, v in cfg.to_dict().items() if k != "PERSISTENT"} == r["cfg"]
+        assert {k: v for k, v in cfg.to_dict().items() if k not in ("PERSISTENT", "CLUSTER")} == r["cfg"]
     for key in RULES["handpicked"].values():
         assert parse_key(key).key() == key
 
@@ -47,13 +47,14 @@ def test_space_size_and_static_prune():
     n = 1
     for v in SPACE.values():
         n *= len(v)
-    assert len(space) == n == 19200
+    assert len(space) == n == 38400
     hw = HwLimits.b200()
     kept, dropped = prune(space, hw)
     assert 0 < len(kept) < len(space)
     assert all(smem_bytes(c) <= hw.smem_per_block_bytes for c in kept)
     assert all(tmem_columns(c) <= 512 for c in kept)
     assert "smem_exceeds_limit" in dropped and "skinny_block_n_not_128_or_256" in dropped
+    assert "cluster_needs_256_rows" in dropped
     assert set(HANDPICKED.values()) <= set(kept)
 
 

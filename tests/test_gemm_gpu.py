@@ -115,6 +115,14 @@ def test_bf16(name):
     MatmulConfig(48, 128, 64, num_stages=4, GROUP_M=1),
     MatmulConfig(128, 128, 64, num_stages=4, PERSISTENT=0),
     MatmulConfig(128, 64, 128, num_stages=4, GROUP_M=4, SPLIT_K=3),
+    MatmulConfig(256, 256, 64, num_stages=6, CLUSTER=2),
+    MatmulConfig(256, 128, 64, num_stages=6, CLUSTER=2),
+    MatmulConfig(256, 256, 128, num_stages=3, num_warps=8, CLUSTER=2),
+    MatmulConfig(256, 192, 64, num_stages=6, CLUSTER=2),
+    MatmulConfig(256, 256, 64, num_stages=6, SPLIT_K=3, GROUP_M=4, CLUSTER=2),
+    MatmulConfig(256, 256, 64, num_stages=6, PERSISTENT=0, CLUSTER=2),
+    MatmulConfig(32, 256, 128, num_stages=6, GROUP_M=1, CLUSTER=2),
+    MatmulConfig(16, 256, 128, num_stages=6, GROUP_M=1, SPLIT_K=2, CLUSTER=2),
 ], ids=lambda c: c.key())
 @pytest.mark.parametrize("shape", [(300, 520, 700), (1024, 1024, 1024), (40, 1000, 3000)])
 def test_knobs_match_oracle(cfg, shape):
@@ -125,7 +133,7 @@ def test_knobs_match_oracle(cfg, shape):
 
 
 @pytest.mark.parametrize("layout", ["a_t", "b_t", "both_t", "a_offset", "b_strided"])
-@pytest.mark.parametrize("name", ["medium", "skinny_m"])
+@pytest.mark.parametrize("name", ["medium", "skinny_m", "large_square"])
 def test_layouts(layout, name):
     """Transposed views read MN-major or K-major in place; unaligned views go through the packing kernel."""
     M, N, K = 200, 256, 320
@@ -184,7 +192,8 @@ def test_square_16384_properties():
     an = a.float().norm(dim=1)
     bn = b.float().norm(dim=0)
     for cfg in (HANDPICKED["large_square"], MatmulConfig(256, 256, 64, num_stages=3, num_warps=8),
-                MatmulConfig(128, 128, 64, num_stages=6, SPLIT_K=2)):
+                MatmulConfig(128, 128, 64, num_stages=6, SPLIT_K=2),
+                MatmulConfig(256, 256, 64, num_stages=6, SPLIT_K=2, CLUSTER=2)):
         run = B200Matmul(cfg).make_runner(a, b)
         c = run()
         torch.cuda.synchronize()

@@ -97,6 +97,9 @@ def static_violations(cfg: MatmulConfig, hw: HwLimits, elem_bytes: int = 2) -> l
     if cfg.CLUSTER == 2 and tm != 256:
         # the pair splits a 256-row tensor-core tile into two 128-row halves
         reasons.append("cluster_needs_256_rows")
+    if cfg.CLUSTER == 2 and not swapped(cfg) and (cfg.BLOCK_N // 2) % 64:
+        # each CTA reads its half of B in 64-column swizzle atoms; other widths would stage B through a copy per call
+        reasons.append("cluster_half_n_not_multiple_of_64")
     if tmem_columns(cfg) > hw.tmem_columns:
         reasons.append("tmem_exceeds_limit")
     if cfg.num_warps == 8 and tn <= 32:

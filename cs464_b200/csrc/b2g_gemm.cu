@@ -252,20 +252,22 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
       int issued = 0;
       bool ok = true;
       const uint32_t tx_bytes = PAIR ? 2u * stage_bytes : stage_bytes;
+      const uint32_t full_leader = PAIR ? map_to_rank(ctl + OFF_FULL, 0) : ctl + OFF_FULL;
       for (int u = first_unit; u < p.units && ok; u += unit_step) {
         const Unit w = decode_unit(p, u);
         const int row_a = w.tm * p.tile_m + static_cast<int>(rank) * p.cta_m;
         const int row_b = w.tn * p.tile_n + static_cast<int>(rank) * p.cta_n;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!wait_phase(ctl + OFF_EMPTY + 8 * s, ph ^ 1u, abort_flag, p.status, p.timeout_ns,
-                          kStatusProducerTimeout)) {
+          const uint32_t empty = ctl + OFF_EMPTY + 8 * s;
+          if (!mbar_try_wait(empty, ph ^ 1u) &&
+              !wait_phase(empty, ph ^ 1u, abort_flag, p.status, p.timeout_ns, kStatusProducerTimeout)) {
             ok = false;
             break;
           }
           const uint32_t full = ctl + OFF_FULL + 8 * s;
           // the pair's leader counts both CTAs' bytes on its own barrier; the peer only issues copies
           if (leader) mbar_arrive_expect_tx(full, tx_bytes);
-          const uint32_t full_c = PAIR ? map_to_rank(full, 0) : full;
+          const uint32_t full_c = full_leader + 8 * s;
           const uint32_t sa = data + s * stage_bytes;
           const uint32_t sb = sa + p.a_stage_bytes;
           const int k0 = kb * p.bk;
@@ -320,16 +322,34 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
       uint32_t ph = 0;
       uint32_t acc = 0, acc_ph = 0;
       bool ok = true;
-      const uint32_t k_atom_a = p.a_mn_major ? 0u : static_cast<uint32_t>(p.cta_m) * 128u;
-      const uint32_t k_atom_b = p.b_mn_major ? 0u : static_cast<uint32_t>(p.cta_n) * 128u;
-      const uint32_t lbo_a = p.a_mn_major ? static_cast<uint32_t>(p.bk) * 128u : 16u;
-      const uint32_t lbo_b = p.b_mn_major ? static_cast<uint32_t>(p.bk) * 128u : 16u;
+      // Descriptors of stage 0 / K step 0 / first 128 rows. Every other (stage, step, half) is a fixed byte offset
+      // added, in 16-byte units, to the start-address field; shared addresses stay below 256 KB so the 14-bit field
+      // never carries into the next one.
+      const uint64_t adesc0 = sdesc_sw128(data, p.a_mn_major ? static_cast<uint32_t>(p.bk) * 128u : 16u, 1024u);
+      const uint64_t bdesc0 =
+          sdesc_sw128(data + p.a_stage_bytes, p.b_mn_major ? static_cast<uint32_t>(p.bk) * 128u : 16u, 1024u);
+      const uint32_t stage16 = stage_bytes >> 4;
+      // K step kk sits at (kk / 4) * step4 + (kk % 4) * step1: MN-major rows of 2048 B per 16 K, K-major 32 B per 16 K
+      // inside a 64-wide swizzle atom and one atom (rows x 128 B) per 64 K.
+      const uint32_t a_step4 = (p.a_mn_major ? 4u * 2048u : static_cast<uint32_t>(p.cta_m) * 128u) >> 4;
+      const uint32_t a_step1 = (p.a_mn_major ? 2048u : 32u) >> 4;
+      const uint32_t b_step4 = (p.b_mn_major ? 4u * 2048u : static_cast<uint32_t>(p.cta_n) * 128u) >> 4;
+      const uint32_t b_step1 = (p.b_mn_major ? 2048u : 32u) >> 4;
+      // second 128 rows of a 256-row single-CTA tile: two 64-row atoms on (MN-major) or 128 rows of 128 B (K-major)
+      const uint32_t a_half16 = (p.a_mn_major ? 2u * static_cast<uint32_t>(p.bk) * 128u : 128u * 128u) >> 4;
+      const bool two_halves = !PAIR && p.tile_m == 256;
       const int ksteps = p.bk / 16;
-      const int halves = PAIR ? 1 : p.tile_m / 128;
+      // commits name each CTA's barrier by its shared::cluster address (the pair's leader signals both CTAs)
+      const uint32_t empty0 = PAIR ? map_to_rank(ctl + OFF_EMPTY, 0) : ctl + OFF_EMPTY;
+      const uint32_t empty1 = PAIR ? map_to_rank(ctl + OFF_EMPTY, 1) : 0u;
+      const uint32_t tfull0 = PAIR ? map_to_rank(ctl + OFF_TFULL, 0) : ctl + OFF_TFULL;
+      const uint32_t tfull1 = PAIR ? map_to_rank(ctl + OFF_TFULL, 1) : 0u;
+      const uint32_t idesc = p.idesc;
       for (int u = first_unit; u < p.units && ok; u += unit_step) {
         const Unit w = decode_unit(p, u);
         if (w.kb0 == w.kb1) continue;
-        if (!wait_phase(ctl + OFF_TEMPTY + 8 * acc, acc_ph ^ 1u, abort_flag, p.status, p.timeout_ns,
+        if (!mbar_try_wait(ctl + OFF_TEMPTY + 8 * acc, acc_ph ^ 1u) &&
+            !wait_phase(ctl + OFF_TEMPTY + 8 * acc, acc_ph ^ 1u, abort_flag, p.status, p.timeout_ns,
                         kStatusMmaTimeout)) {
           ok = false;
           break;
@@ -337,33 +357,35 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
         tc_fence_after();
         const uint32_t d_base = tmem_base + acc * p.acc_cols;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!wait_phase(ctl + OFF_FULL + 8 * s, ph, abort_flag, p.status, p.timeout_ns, kStatusMmaTimeout)) {
+          const uint32_t full = ctl + OFF_FULL + 8 * s;
+          // TMA data is ordered by the barrier's byte count (both are async-proxy operations): no tcgen05 fence here
+          if (!mbar_try_wait(full, ph) &&
+              !wait_phase(full, ph, abort_flag, p.status, p.timeout_ns, kStatusMmaTimeout)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint32_t sa = data + s * stage_bytes;
-          const uint32_t sb = sa + p.a_stage_bytes;
-          for (int kk = 0; kk < ksteps; ++kk) {
-            // K offset of this 16-wide step inside the operand tile
-            const uint32_t a_k = p.a_mn_major ? kk * 2048u : (kk >> 2) * k_atom_a + (kk & 3) * 32u;
-            const uint32_t b_k = p.b_mn_major ? kk * 2048u : (kk >> 2) * k_atom_b + (kk & 3) * 32u;
-            const uint64_t bdesc = sdesc_sw128(sb + b_k, lbo_b, 1024u);
-            for (int h = 0; h < halves; ++h) {
-              // rows 128h.. of a 256-row A tile: two 64-row atoms on for MN-major, 128 swizzled rows on for K-major
-              const uint32_t a_h = p.a_mn_major ? h * 2u * static_cast<uint32_t>(p.bk) * 128u : h * 128u * 128u;
-              const uint64_t adesc = sdesc_sw128(sa + a_h + a_k, lbo_a, 1024u);
-              const uint32_t accumulate = (kb > w.kb0 || kk > 0) ? 1u : 0u;
-              if (PAIR) umma_f16_pair(d_base, adesc, bdesc, p.idesc, accumulate);
-              else umma_f16(d_base + h * p.tile_n, adesc, bdesc, p.idesc, accumulate);
+          const uint64_t a_s = adesc0 + s * stage16;
+          const uint64_t b_s = bdesc0 + s * stage16;
+          const uint32_t first = (kb == w.kb0) ? 0u : 1u;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            if (kk < ksteps) {
+              const uint64_t ad = a_s + ((kk >> 2) * a_step4 + (kk & 3) * a_step1);
+              const uint64_t bd = b_s + ((kk >> 2) * b_step4 + (kk & 3) * b_step1);
+              const uint32_t accumulate = kk == 0 ? first : 1u;
+              if (PAIR) {
+                umma_f16_pair(d_base, ad, bd, idesc, accumulate);
+              } else {
+                umma_f16(d_base, ad, bd, idesc, accumulate);
+                if (two_halves) umma_f16(d_base + p.tile_n, ad + a_half16, bd, idesc, accumulate);
+              }
             }
           }
           if (PAIR) {
-            const uint32_t e = ctl + OFF_EMPTY + 8 * s;
-            umma_commit_pair(map_to_rank(e, 0));
-            umma_commit_pair(map_to_rank(e, 1));
+            umma_commit_pair(empty0 + 8 * s);
+            umma_commit_pair(empty1 + 8 * s);
           } else {
-            umma_commit(ctl + OFF_EMPTY + 8 * s);
+            umma_commit(empty0 + 8 * s);
           }
           if (++s == p.stages) {
             s = 0;
@@ -372,11 +394,10 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
         }
         if (!ok) break;
         if (PAIR) {
-          const uint32_t f = ctl + OFF_TFULL + 8 * acc;
-          umma_commit_pair(map_to_rank(f, 0));
-          umma_commit_pair(map_to_rank(f, 1));
+          umma_commit_pair(tfull0 + 8 * acc);
+          umma_commit_pair(tfull1 + 8 * acc);
         } else {
-          umma_commit(ctl + OFF_TFULL + 8 * acc);
+          umma_commit(tfull0 + 8 * acc);
         }
         if (++acc == p.num_acc) {
           acc = 0;

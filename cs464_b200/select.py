@@ -24,7 +24,7 @@ def heuristic_config(M: int, N: int, K: int, sm_count: int = SM_COUNT) -> Matmul
         return MatmulConfig(bm, 128, 128, num_warps=4, num_stages=stages, GROUP_M=1, SPLIT_K=split)
     tiles_big = -(-M // 256) * -(-N // 256)
     if tiles_big >= sm_count // 2:
-        return MatmulConfig(256, 256, 64, num_warps=8, num_stages=3, GROUP_M=8)
+        return MatmulConfig(256, 256, 64, num_warps=4, num_stages=3, GROUP_M=8)
     tiles = -(-M // 128) * -(-N // 128)
     split = 1
     kb = -(-K // 64)

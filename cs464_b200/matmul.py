@@ -190,3 +190,39 @@ class B200Matmul:
 
 def matmul(a: torch.Tensor, b: torch.Tensor, cfg: MatmulConfig) -> torch.Tensor:
     return B200Matmul(cfg).make_runner(a, b)()
+
+
+_ABI_CFG: dict = {}
+_STATUS: dict = {}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """A per-device int32 status word shared by one-shot launches (`gemm`)."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    t = _STATUS.get(key)
+    if t is None:
+        t = _STATUS[key] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", key))
+    return t
+
+
+def gemm(cfg: MatmulConfig, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """One-shot C = A @ B on the current stream through `b2g_gemm` (plan, launch and free in one C call): the lean path
+    for per-call dispatch, where building a runner object per call would cost more host time than small kernels
+    take. The output is fresh each call unless `out` is given."""
+    M, K = a.shape
+    N = b.shape[1]
+    c = out if out is not None else torch.empty((M, N), device=a.device, dtype=a.dtype)
+    acfg = _ABI_CFG.get(cfg)
+    if acfg is None:
+        acfg = _ABI_CFG[cfg] = cfg.to_abi()
+    lib = _abi.load()
+    pr = problem(M, N, K, a.stride(), b.stride(), c.stride(), a.dtype)
+    n = ctypes.c_size_t(0)
+    _abi.check(lib.b2g_workspace_size(ctypes.byref(acfg), ctypes.byref(pr), a.data_ptr(), b.data_ptr(),
+                                      ctypes.byref(n)), "b2g_workspace_size")
+    ws = torch.empty(n.value, dtype=torch.uint8, device=a.device) if n.value else None
+    rc = lib.b2g_gemm(ctypes.byref(acfg), ctypes.byref(pr), a.data_ptr(), b.data_ptr(), c.data_ptr(),
+                      ws.data_ptr() if ws is not None else None, n.value, status_word(a.device).data_ptr(),
+                      torch.cuda.current_stream(a.device).cuda_stream)
+    _abi.check(rc, "b2g_gemm")
+    return c

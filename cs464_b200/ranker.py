@@ -1,0 +1,194 @@
+"""Candidate ranking for the online search: which configs of the sm_100a space to time for a new shape.
+
+The reference ranks its Triton pool with a LightGBM model over config and shape features (analysis/learned.py:461-535,
+features analysis/selectors.py:130-151 and analysis/learned.py:264-285, with RTX 3080 roofline constants at :242). Its
+models rank Triton keys, so they cannot rank this family; lightgbm is not installed here either. This module keeps
+the ranker interface (`rank(M, N, K, k, order)`, `scores`, `cfgs`, `pool_keys`, `load`) with two rankers:
+  * `AnalyticRanker`: a roofline model of this kernel on B200 (waves over 148 SMs, tensor time per tile, L2->SM and
+    HBM bytes, per-K-step issue overhead, split-K and staging costs); needs no training data;
+  * `LearnedRanker`: gradient-boosted trees (scikit-learn) over the same features, fitted on measured screens of
+    this family on B200 (`fit(rows)`), saved as <stem>.pkl + <stem>.json.
+"""
+from __future__ import annotations
+
+import json
+import math
+from pathlib import Path
+
+import numpy as np
+
+from cs464_b200.config_space import HwLimits, full_space, mma_tile, prune, shape_violations, smem_bytes, swapped
+from cs464_b200.matmul import MatmulConfig
+
+# B200 model constants (per GPU, as measured on this pool: MEASURED_PEAKS.json)
+PEAK_FLOPS = 1.63e15
+HBM_BPS = 6.55e12
+SM_COUNT = 148
+CLOCK_HZ = 1.85e9
+L2_BYTES_PER_CLK_PER_SM = 64.0
+KBLOCK_OVERHEAD_CLK = 110.0
+LAUNCH_S = 3.0e-6
+EXTRA_KERNEL_S = 2.0e-6
+
+
+def config_params(cfg: MatmulConfig) -> dict:
+    """The tunables as numbers (the reference's config_params, analysis/learned.py:75-79, plus the new knobs)."""
+    return {k: float(v) for k, v in cfg.to_dict().items()}
+
+
+def _geometry(M: int, N: int, K: int, cfg: MatmulConfig) -> dict:
+    tm, tn = mma_tile(cfg)
+    rows_a, rows_b = (N, M) if swapped(cfg) else (M, N)
+    tiles_m = -(-rows_a // tm)
+    tiles_n = -(-rows_b // tn)
+    nkb = max(1, -(-K // cfg.BLOCK_K))
+    split = cfg.SPLIT_K
+    units = tiles_m * tiles_n * split
+    sms_per_unit = 2 if cfg.CLUSTER == 2 else 1
+    slots = SM_COUNT // sms_per_unit if cfg.PERSISTENT else units
+    waves = units / max(1, SM_COUNT // sms_per_unit)
+    return {"tm": tm, "tn": tn, "rows_a": rows_a, "rows_b": rows_b, "tiles_m": tiles_m, "tiles_n": tiles_n,
+            "nkb": nkb, "kb_per_unit": -(-nkb // split), "units": units, "sms_per_unit": sms_per_unit,
+            "slots": slots, "waves": waves, "fill_m": rows_a / (tiles_m * tm), "fill_n": rows_b / (tiles_n * tn)}
+
+
+def analytic_time_s(M: int, N: int, K: int, cfg: MatmulConfig) -> float:
+    """Predicted kernel time of `cfg` on a row-major (M, N, K) problem (seconds)."""
+    g = _geometry(M, N, K, cfg)
+    per_sm_flops_clk = PEAK_FLOPS / SM_COUNT / CLOCK_HZ
+    # tensor work of one K block on one SM (a pair splits the tile's rows over two SMs)
+    mma_n_eff = min(1.0, g["tn"] / 64.0) ** 0.5  # narrow N wastes tensor issue slots
+    kb_flops = 2.0 * g["tm"] * g["tn"] * cfg.BLOCK_K / g["sms_per_unit"]
+    t_mma = kb_flops / (per_sm_flops_clk * max(mma_n_eff, 0.25))
+    kb_bytes = (g["tm"] + g["tn"]) * cfg.BLOCK_K * 2.0 / g["sms_per_unit"]
+    t_load = kb_bytes / L2_BYTES_PER_CLK_PER_SM
+    per_kb = max(t_mma, t_load) + KBLOCK_OVERHEAD_CLK
+    # pipeline latency cover: a shallow ring stalls on load latency
+    ring_clk = cfg.num_stages * max(t_mma, t_load)
+    per_kb += max(0.0, 2500.0 - ring_clk) / cfg.num_stages
+    unit_clk = g["kb_per_unit"] * per_kb
+    acc_cols = g["tn"] if cfg.CLUSTER == 2 else (g["tm"] // 128) * g["tn"]
+    epi_clk = g["tm"] * g["tn"] * (2.0 if cfg.SPLIT_K == 1 else 4.0) / g["sms_per_unit"] / (16.0 * cfg.num_warps)
+    if 2 * acc_cols > 512:  # single accumulator: the epilogue does not overlap the next tile's main loop
+        unit_clk += epi_clk
+    waves = math.ceil(g["units"] / max(1, g["slots"])) if cfg.PERSISTENT else math.ceil(g["waves"])
+    t = waves * unit_clk / CLOCK_HZ + (0.0 if 2 * acc_cols > 512 else epi_clk / CLOCK_HZ)
+    # DRAM floor: compulsory operand bytes (B re-read per tile row group is assumed to hit L2)
+    dram = 2.0 * (M * K + K * N + M * N)
+    if cfg.SPLIT_K > 1:
+        dram += 4.0 * cfg.SPLIT_K * M * N * 2 + 2.0 * M * N
+    t = max(t, dram / HBM_BPS)
+    t += LAUNCH_S + (EXTRA_KERNEL_S if cfg.SPLIT_K > 1 else 0.0)
+    return t
+
+
+def candidate_features(M: int, N: int, K: int, cfg: MatmulConfig) -> dict:
+    """Shape + config + derived features (tile fill, waves, per-unit work, analytic terms), all numeric."""
+    g = _geometry(M, N, K, cfg)
+    f = {"log2_M": math.log2(M), "log2_N": math.log2(N), "log2_K": math.log2(K),
+         "log2_MNK": math.log2(M) + math.log2(N) + math.log2(K), **config_params(cfg),
+         "swapped": float(swapped(cfg)), "smem_kib": smem_bytes(cfg) / 1024.0, "fill_m": g["fill_m"],
+         "fill_n": g["fill_n"], "waves": g["waves"], "waves_frac": g["waves"] - math.floor(g["waves"]),
+         "log2_units": math.log2(g["units"]), "kb_per_unit": float(g["kb_per_unit"]),
+         "log_analytic_us": math.log(analytic_time_s(M, N, K, cfg) * 1e6),
+         "log_dram_floor_us": math.log(2.0 * (M * K + K * N + M * N) / HBM_BPS * 1e6 + 1e-3),
+         "log_tensor_floor_us": math.log(2.0 * M * N * K / PEAK_FLOPS * 1e6 + 1e-3)}
+    return f
+
+
+FEATURES = list(candidate_features(64, 64, 64, MatmulConfig(128, 128, 64)).keys())
+
+
+class AnalyticRanker:
+    """Ranks the statically pruned space by the analytic time model (lower = better)."""
+
+    kind = "analytic"
+
+    def __init__(self, pool: list[MatmulConfig] | None = None, hw: HwLimits | None = None):
+        self.hw = hw or HwLimits.b200()
+        self.cfgs = pool if pool is not None else prune(full_space(), self.hw)[0]
+        self.pool_keys = [c.key() for c in self.cfgs]
+        self.stem = None
+
+    def scores(self, M: int, N: int, K: int) -> np.ndarray:
+        return np.array([math.log(analytic_time_s(M, N, K, c)) for c in self.cfgs])
+
+    def rank(self, M: int, N: int, K: int, k: int, order: str = "plain") -> list[str]:
+        """Top-k keys among configs with no shape violation. "diverse" takes at most one config per tile
+        (BLOCK_M, BLOCK_N, BLOCK_K, SPLIT_K, CLUSTER) before repeating any tile."""
+        s = self.scores(M, N, K)
+        idx = [i for i in np.argsort(s, kind="stable") if not shape_violations(self.cfgs[i], M, N, K)]
+        if order == "plain":
+            return [self.pool_keys[i] for i in idx[:k]]
+        out, seen, rest = [], set(), []
+        for i in idx:
+            c = self.cfgs[i]
+            tile = (c.BLOCK_M, c.BLOCK_N, c.BLOCK_K, c.SPLIT_K, c.CLUSTER)
+            if tile in seen:
+                rest.append(i)
+                continue
+            seen.add(tile)
+            out.append(i)
+            if len(out) == k:
+                break
+        out += rest[: k - len(out)]
+        return [self.pool_keys[i] for i in out]
+
+
+class LearnedRanker(AnalyticRanker):
+    """Gradient-boosted trees over `candidate_features`, predicting log(time / best time of the shape)."""
+
+    kind = "learned"
+
+    def __init__(self, model=None, pool: list[MatmulConfig] | None = None, hw: HwLimits | None = None):
+        super().__init__(pool, hw)
+        self.model = model
+
+    @staticmethod
+    def _matrix(M: int, N: int, K: int, cfgs: list[MatmulConfig]) -> np.ndarray:
+        return np.array([[candidate_features(M, N, K, c)[f] for f in FEATURES] for c in cfgs], dtype=np.float64)
+
+    def fit(self, rows: list[dict], **kw) -> "LearnedRanker":
+        """rows: {"M", "N", "K", "key", "us"} timings of valid candidates (several per shape)."""
+        from sklearn.ensemble import HistGradientBoostingRegressor
+
+        from cs464_b200.keys import parse_key
+        best: dict[tuple, float] = {}
+        for r in rows:
+            s = (r["M"], r["N"], r["K"])
+            best[s] = min(best.get(s, math.inf), r["us"])
+        X = np.array([[candidate_features(r["M"], r["N"], r["K"], parse_key(r["key"]))[f] for f in FEATURES]
+                      for r in rows])
+        y = np.array([math.log(r["us"] / best[(r["M"], r["N"], r["K"])]) for r in rows])
+        params = {"max_iter": 400, "learning_rate": 0.06, "max_leaf_nodes": 48, "l2_regularization": 1e-3}
+        params.update(kw)
+        self.model = HistGradientBoostingRegressor(**params).fit(X, y)
+        return self
+
+    def scores(self, M: int, N: int, K: int) -> np.ndarray:
+        if self.model is None:
+            return super().scores(M, N, K)
+        return self.model.predict(self._matrix(M, N, K, self.cfgs))
+
+    def save(self, stem: str | Path) -> None:
+        import pickle
+        stem = Path(stem)
+        stem.parent.mkdir(parents=True, exist_ok=True)
+        with open(f"{stem}.pkl", "wb") as f:
+            pickle.dump(self.model, f)
+        Path(f"{stem}.json").write_text(json.dumps({"features": FEATURES, "pool": self.pool_keys}))
+        self.stem = str(stem)
+
+    @classmethod
+    def load(cls, stem: str | Path) -> "LearnedRanker":
+        import pickle
+
+        from cs464_b200.keys import parse_key
+        meta = json.loads(Path(f"{stem}.json").read_text())
+        if meta["features"] != FEATURES:
+            raise ValueError(f"{stem}: feature list differs from this version's; retrain")
+        with open(f"{stem}.pkl", "rb") as f:
+            model = pickle.load(f)
+        r = cls(model, [parse_key(k) for k in meta["pool"]])
+        r.stem = str(stem)
+        return r

@@ -1,0 +1,242 @@
+"""Host logic of the hot path's callers, on CPU: gate, timing statistics, winner cache, ranker, candidate expansion,
+choice, dispatch rule and shape suites (the reference tests these the same way, with fakes and no GPU:
+tests/test_winner_cache.py, tests/test_online_split.py, tests/test_timing.py:10-26)."""
+from __future__ import annotations
+
+import json
+import math
+import multiprocessing as mp
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from cs464_b200 import dispatch, gate, suites, timing
+from cs464_b200.config_space import shape_violations
+from cs464_b200.keys import parse_key
+from cs464_b200.matmul import MatmulConfig
+from cs464_b200.ranker import AnalyticRanker, LearnedRanker, analytic_time_s, candidate_features
+from cs464_b200.search import KPolicy, candidates_for, choose, shape_space
+from cs464_b200.winner_cache import WinnerCache, backend_for, tier
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+ENV = {"hw_id": "NVIDIA B200|sm100|148sm|179GiB", "kernel_src": "abc", "torch": "2.11", "cuda_runtime": "12.8",
+       "driver": "580.159", "clock_lock": None}
+
+
+# ---------------------------------------------------------------- gate
+def test_gate_verdicts_match_reference_fixtures():
+    z = np.load(GOLDEN / "gemm_cases.npz")
+    for case in json.loads((GOLDEN / "gemm_cases.json").read_text())["cases"]:
+        dt = getattr(torch, case["dtype"])
+        ref = torch.from_numpy(z[f"{case['name']}_ref"])
+        r = gate.check_output(ref.to(dt), ref, case["K"], dt)
+        assert r.valid == case["verdicts"]["rounded"]["valid"]
+        nan = ref.to(dt).clone()
+        nan[-1] = float("nan")
+        r = gate.check_output(nan, ref, case["K"], dt)
+        assert r.failure_reason == case["verdicts"]["nan_row"]["failure_reason"]
+
+
+def test_gate_norm_relative_bound():
+    a, b = gate.make_inputs(32, 24, 128, device="cpu")
+    ref = gate.reference(a, b)
+    assert gate.check_norm_relative(ref.half(), ref, a, b).valid
+    bad = ref.clone()
+    bad[1, 2] += 0.5
+    r = gate.check_norm_relative(bad.half(), ref, a, b)
+    assert not r.valid and r.failure_reason == "norm_relative_exceeded"
+
+
+def test_gate_validate_turns_exceptions_into_failures():
+    class Boom:
+        def make_runner(self, a, b, out=None):
+            raise RuntimeError("unsupported: smem_exceeds_limit")
+    a, b = gate.make_inputs(8, 8, 8, device="cpu")
+    r = gate.validate(Boom(), 8, 8, 8, inputs=(a, b), ref=gate.reference(a, b))
+    assert not r.valid and "unsupported" in r.failure_reason
+    assert gate.context_poisoned("CUDA error: an illegal memory access was encountered")
+    assert not gate.context_poisoned("unsupported: smem_exceeds_limit")
+
+
+def test_make_inputs_scale_b():
+    a1, b1 = gate.make_inputs(4, 6, 8, device="cpu")
+    a2, b2 = gate.make_inputs(4, 6, 8, device="cpu", scale_b=0.02)
+    assert torch.equal(a1, a2)
+    assert torch.allclose(b2.float(), (b1.float() * 0.02), rtol=2e-3, atol=1e-5)
+
+
+# ---------------------------------------------------------------- timing
+def test_timing_config_rules_and_stats():
+    with pytest.raises(ValueError):
+        timing.TimingConfig(cache_mode="cold", batch=4)
+    with pytest.raises(ValueError):
+        timing.TimingConfig(cache_mode="warm")
+    s = timing.summarize([10.0, 11.0, 9.0, 10.0])
+    assert s["median_us"] == 10.0 and s["n_samples"] == 4 and s["rse"] < 0.1
+    r1 = timing.TimingResult(**timing.summarize([1, 2, 3]), cache_mode="cold", batch=1, use_graph=False, wall_s=1,
+                             samples_us=[1, 2, 3])
+    r2 = timing.TimingResult(**timing.summarize([4, 5]), cache_mode="cold", batch=1, use_graph=False, wall_s=2,
+                             samples_us=[4, 5])
+    p = timing.pool([r1, r2])
+    assert p.n_samples == 5 and p.median_us == 3 and p.wall_s == 3
+    cold, graph = timing.short_configs()
+    assert cold.max_reps == 10 and graph.use_graph and graph.batch == 20
+
+
+# ---------------------------------------------------------------- winner cache
+def test_winner_cache_round_trip_and_tiers(tmp_path):
+    p = tmp_path / "wc.jsonl"
+    wc = WinnerCache(p, env=ENV)
+    assert wc.get(1, 2, 3) is None
+    wc.put(64, 64, 64, "fp16", k=3, choice={"key": "bm128_bn128_bk64_w4_s6_g8_sk1", "us": 5.0})
+    assert wc.get(64, 64, 64, "fp16", k=3)["choice"]["us"] == 5.0
+    assert wc.get(64, 64, 64, "fp16", k=5) is None            # a narrower search does not serve a wider request
+    assert WinnerCache(p, env=ENV).get(64, 64, 64, "fp16")["stale"] == []
+    soft = WinnerCache(p, env={**ENV, "driver": "999"})
+    assert soft.get(64, 64, 64, "fp16") is None
+    assert soft.get(64, 64, 64, "fp16", allow_stale=True)["stale"] == ["driver"]
+    assert WinnerCache(p, env={**ENV, "kernel_src": "new"}).get(64, 64, 64, "fp16", allow_stale=True) is None
+    assert WinnerCache(p, env={**ENV, "hw_id": "other"}).get(64, 64, 64, "fp16", allow_stale=True) is None
+    assert tier({"env": {"hw_id": "x"}}, {"hw_id": "y", "torch": None})[0] == "hard"
+
+
+def test_winner_cache_torn_line_and_compact(tmp_path):
+    p = tmp_path / "wc.jsonl"
+    wc = WinnerCache(p, env=ENV)
+    wc.put(8, 8, 8, "fp16", k=1, choice={"key": "bm128_bn128_bk64_w4_s6_g8_sk1", "us": 3.0})
+    with open(p, "a") as f:
+        f.write('{"schema": 1, "M": 9, "N"')        # a crash mid-write
+    wc2 = WinnerCache(p, env=ENV)
+    wc2.put(16, 16, 16, "fp16", k=1, choice={"key": "bm128_bn64_bk64_w4_s8_g8_sk1", "us": 4.0})
+    wc3 = WinnerCache(p, env=ENV)
+    assert wc3.get(8, 8, 8)["choice"]["us"] == 3.0 and wc3.get(16, 16, 16)["choice"]["us"] == 4.0
+    for i in range(5):
+        wc3.put(8, 8, 8, "fp16", k=1, choice={"key": "bm128_bn128_bk64_w4_s6_g8_sk1", "us": float(i)})
+    st = wc3.compact()
+    assert st["after"] == 2 and WinnerCache(p, env=ENV).get(8, 8, 8)["choice"]["us"] == 4.0
+
+
+def _puts(path, rank, n):
+    wc = WinnerCache(path, env=ENV)
+    for i in range(n):
+        wc.put(rank * 1000 + i, 8, 8, "fp16", k=1, choice={"key": "bm128_bn128_bk64_w4_s6_g8_sk1", "us": 1.0})
+
+
+def test_winner_cache_concurrent_puts_lose_nothing(tmp_path):
+    p = tmp_path / "wc.jsonl"
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_puts, args=(str(p), r, 40)) for r in range(3)]
+    for x in procs:
+        x.start()
+    for x in procs:
+        x.join()
+        assert x.exitcode == 0
+    assert len(WinnerCache(p, env=ENV)) == 120
+
+
+def test_backend_for_builds_from_keys():
+    be = backend_for({"key": "bm256_bn256_bk64_w4_s3_g8_sk1_c2"})
+    assert be.cfg == MatmulConfig(256, 256, 64, num_stages=3, CLUSTER=2)
+    assert backend_for({"key": None}) is None
+    assert backend_for({"key": "default", "family": "torch_matmul"}).family == "torch_matmul"
+    with pytest.raises(ValueError):
+        backend_for({"key": "bm1_bad"})
+
+
+# ---------------------------------------------------------------- ranker, candidates, choice
+def test_analytic_ranker_prefers_sensible_configs():
+    r = AnalyticRanker()
+    top = [parse_key(k) for k in r.rank(8192, 8192, 8192, 5)]
+    assert all(c.BLOCK_M >= 128 and c.SPLIT_K == 1 for c in top)
+    skinny = [parse_key(k) for k in r.rank(1, 28672, 4096, 5)]
+    assert all(c.BLOCK_M <= 64 for c in skinny)
+    for k in r.rank(100, 70, 1000, 8, order="diverse"):
+        assert not shape_violations(parse_key(k), 100, 70, 1000)
+    div = [parse_key(k) for k in r.rank(4096, 4096, 4096, 6, order="diverse")]
+    assert len({(c.BLOCK_M, c.BLOCK_N, c.BLOCK_K, c.SPLIT_K, c.CLUSTER) for c in div}) == 6
+    assert analytic_time_s(4096, 4096, 4096, MatmulConfig(256, 256, 64)) > 2 * 4096 ** 3 / 1.63e15
+
+
+def test_learned_ranker_fit_save_load(tmp_path):
+    rng = np.random.default_rng(0)
+    pool = shape_space(512, 512, 512)[:40]
+    rows = []
+    for (M, N, K) in [(512, 512, 512), (64, 4096, 1024), (2048, 1024, 4096)]:
+        for c in pool[:30]:
+            rows.append({"M": M, "N": N, "K": K, "key": c.key(),
+                         "us": analytic_time_s(M, N, K, c) * 1e6 * float(rng.uniform(0.9, 1.1))})
+    lr = LearnedRanker(pool=pool).fit(rows, max_iter=30)
+    lr.save(tmp_path / "rk")
+    lr2 = LearnedRanker.load(tmp_path / "rk")
+    assert lr2.pool_keys == lr.pool_keys
+    assert np.allclose(lr2.scores(512, 512, 512), lr.scores(512, 512, 512))
+    assert len(lr2.rank(512, 512, 512, 3)) == 3
+    assert set(candidate_features(1, 2, 3, pool[0])) >= {"log2_M", "BLOCK_M", "waves", "log_analytic_us"}
+
+
+def test_candidates_for_specs():
+    assert [c.config_key for c in candidates_for("b200:handpicked", 1024, 1024, 1024)]
+    one = candidates_for("b200:bm256_bn256_bk64_w4_s3_g8_sk1", 1024, 1024, 1024)
+    assert len(one) == 1 and one[0].family == "b200_sm100a_v1"
+    assert len(candidates_for("b200:rank:4", 512, 512, 512)) == 4
+    assert 0 < len(candidates_for("b200:space:50", 512, 512, 512)) <= 50
+    assert candidates_for("torch", 8, 8, 8)[0].family == "torch_matmul"
+    big_split = MatmulConfig(128, 128, 64, SPLIT_K=16).key()
+    assert candidates_for(f"b200:{big_split}", 16384, 16384, 16384) == []  # workspace too large is a hard drop
+    with pytest.raises(ValueError):
+        candidates_for("triton:handpicked", 8, 8, 8)
+
+
+def test_choose_and_policy():
+    cands = [{"config_key": "a", "valid": True, "cold_us": 120.0}, {"config_key": "b", "valid": True, "cold_us": 100.0},
+             {"config_key": "c", "valid": False}]
+    assert choose(cands)["key"] == "b" and choose(cands)["mode"] == "cold"
+    assert choose(cands, k=1)["key"] == "a"
+    small = [{"config_key": "a", "valid": True, "cold_us": 20.0, "graph_us": 9.0},
+             {"config_key": "b", "valid": True, "cold_us": 19.0, "graph_us": 10.0}]
+    assert choose(small)["key"] == "a" and choose(small)["mode"] == "graph"
+    assert choose([{"config_key": "x", "valid": False}])["key"] is None
+    assert KPolicy().k_for() == 3 and KPolicy().k_for(calls=2_000_000) == 5 and KPolicy().k_for(frequent=True) == 5
+
+
+def test_dispatch_rule():
+    e = {"torch_us": 100.0, "choice": {"us": 90.0}, "env": {"clock_lock": None}}
+    assert dispatch.dispatch_rule(e)
+    assert not dispatch.dispatch_rule({**e, "choice": {"us": 97.0}})           # saves 3 % < 4 %
+    big = {"torch_us": 1000.0, "choice": {"us": 965.0}}
+    assert not dispatch.dispatch_rule({**big, "env": {"clock_lock": None}})       # unlocked needs 4 % = 40 us
+    assert dispatch.dispatch_rule({**big, "env": {"clock_lock": "1800"}})         # a declared lock needs 3 % = 30 us
+    assert not dispatch.dispatch_rule({"torch_us": 8.0, "choice": {"us": 1.0}})   # below min_kernel_us
+    assert not dispatch.dispatch_rule({"choice": {"us": 1.0}})                    # no torch time: never
+
+
+def test_dispatch_enable_disable_leaves_cpu_calls_to_torch(tmp_path):
+    wc = WinnerCache(tmp_path / "wc.jsonl", env=ENV)
+    orig = torch.matmul
+    dispatch.enable(cache=wc)
+    try:
+        assert dispatch.is_enabled() and torch.matmul is not orig
+        a = torch.randn(4, 5)
+        b = torch.randn(5, 3)
+        assert torch.allclose(torch.matmul(a, b), a @ b) and torch.allclose(torch.mm(a, b), a.mm(b))
+        assert dispatch.stats()["torch"] >= 2 and dispatch.stats()["routed"] == 0
+    finally:
+        dispatch.disable()
+    assert torch.matmul is orig and not dispatch.is_enabled()
+
+
+# ---------------------------------------------------------------- suites
+def test_suites():
+    r = suites.random_suite()
+    assert len(r) == 200 and sum(1 for s in r if s.get("skinny")) == 40
+    assert all(s["M"] % 8 == 0 and 16 <= s["M"] <= 16384 and s["N"] % 8 == 0 and s["K"] % 8 == 0 for s in r)
+    assert all(s["M"] <= 64 for s in r if s.get("skinny"))
+    assert r == suites.random_suite()
+    assert len(suites.fresh_suite()) == 1000 and suites.fresh_suite()[:5] != r[:5]
+    ll = suites.llama_suite()
+    assert len(ll) == 20 and {(s["K"], s["N"]) for s in ll} == {(4096, 6144), (4096, 4096), (4096, 28672),
+                                                                 (14336, 4096)}
+    for name in suites.SUITES:
+        assert suites.load(name) == json.loads((suites.DATA / f"{name}.json").read_text())["shapes"]

@@ -1,0 +1,138 @@
+"""GPU tests of the hot path's callers driving the sm_100a family: gate sensitivity (the reference's
+tests/test_correctness.py), timer accuracy (tests/test_timing.py), first-use selection with the winner cache, the
+full-space screen, one sharded-search step, and torch.matmul routing."""
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from cs464_b200 import dispatch, gate
+from cs464_b200.baselines import TorchMatmul
+from cs464_b200.config_space import HANDPICKED
+from cs464_b200.matmul import B200Matmul, MatmulConfig
+from cs464_b200.search import screen_shape, select_kernel, shape_space
+from cs464_b200.timing import TimingConfig, benchmark
+from cs464_b200.winner_cache import WinnerCache, environment
+
+pytestmark = pytest.mark.gpu
+
+
+class _Fn:
+    def __init__(self, fn):
+        self.fn = fn
+
+    def make_runner(self, a, b, out=None):
+        return lambda: self.fn(a, b, out)
+
+
+def test_gate_passes_the_family_and_catches_mistakes():
+    assert gate.validate(B200Matmul(HANDPICKED["medium"]), 129, 257, 1031, norm_rel=True).valid
+
+    def bad_tile(a, b, out):
+        gate.reference(a, b).to(out.dtype).clone()
+        out.copy_(a @ b)
+        out[64:80, 32:48] += 1.0
+        return out
+    r = gate.validate(_Fn(bad_tile), 128, 128, 4096)
+    assert not r.valid and r.failure_reason == "tolerance_exceeded"
+
+    def partial(a, b, out):
+        out[:-1] = a[:-1] @ b
+        return out
+    r = gate.validate(_Fn(partial), 65, 64, 64)
+    assert not r.valid and r.failure_reason.startswith("non_finite")
+
+
+def test_fp16_accumulation_error_far_above_fp32_accumulation():
+    M, N, K = 64, 64, 16384
+    a, b = gate.make_inputs(M, N, K)
+    ref = gate.reference(a, b)
+
+    def fp16_acc(a, b):
+        acc = torch.zeros(M, N, device=a.device, dtype=torch.float16)
+        for k in range(0, K, 16):
+            acc += a[:, k:k + 16] @ b[k:k + 16]
+        return acc
+    ours = B200Matmul(HANDPICKED["large_k_splitk"]).make_runner(a, b)()
+    rms = lambda c: float((c.float() - ref).pow(2).mean().sqrt())  # noqa: E731
+    assert rms(fp16_acc(a, b)) > 5 * rms(ours)
+
+
+def test_timer_recovers_a_known_sleep():
+    cycles_per_us = None
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(1000)
+    s.record()
+    torch.cuda._sleep(10_000_000)
+    e.record()
+    e.synchronize()
+    cycles_per_us = 10_000_000 / (s.elapsed_time(e) * 1e3)
+    n = int(200 * cycles_per_us)
+    r = benchmark(lambda: torch.cuda._sleep(n), TimingConfig(cache_mode="hot", max_reps=50))
+    assert 150 <= r.median_us <= 260, r.median_us
+
+
+def test_graph_and_hot_modes_on_the_family():
+    a, b = gate.make_inputs(1024, 1024, 1024)
+    run = B200Matmul(MatmulConfig(128, 128, 64, num_stages=6)).make_runner(a, b)
+    single = benchmark(run, TimingConfig(cache_mode="hot", max_reps=50)).median_us
+    graph = benchmark(run, TimingConfig(cache_mode="hot", batch=20, use_graph=True, max_reps=20)).median_us
+    cold = benchmark(run, TimingConfig(cache_mode="cold", max_reps=30)).median_us
+    assert graph <= single * 1.1
+    assert single <= cold * 1.05
+
+
+def test_select_kernel_searches_then_hits_the_cache(tmp_path):
+    wc = WinnerCache(tmp_path / "wc.jsonl", env=environment())
+    r1 = select_kernel(None, 777, 512, 1024, cache=wc)
+    assert not r1["cached"] and r1["choice"]["key"] is not None and len(r1["candidates"]) == 3
+    assert all(c["valid"] for c in r1["candidates"]), r1["candidates"]
+    r2 = select_kernel(None, 777, 512, 1024, cache=wc)
+    assert r2["cached"] and r2["choice"]["key"] == r1["choice"]["key"]
+    r3 = select_kernel(None, 777, 512, 1024, cache=wc, frequent=True)  # wider search than the cached one: searched
+    assert not r3["cached"] and len(r3["candidates"]) == 5
+
+
+def test_screen_shape_small_pool():
+    pool = shape_space(512, 512, 512)[::97][:12]
+    s = screen_shape(512, 512, 512, pool)
+    assert s["best_key"] is not None and s["n_configs"] == len(pool)
+    assert all(r["status"] in ("ok", "slow") or r["status"].startswith("invalid") for r in s["rows"])
+    assert all(not r["status"].startswith("invalid") for r in s["rows"]), s["rows"]
+
+
+def test_sharded_search_step():
+    from cs464_b200.shard import search_one
+    row = search_one({"M": 96, "N": 640, "K": 512}, k=3, space=10)
+    assert row["best_key"] is not None and row["gap"] is not None and row["gap"] >= 0.0
+    assert row["n_screened"] >= 10
+
+
+def test_dispatch_routes_a_cached_winner(tmp_path):
+    wc = WinnerCache(tmp_path / "wc.jsonl", env=environment())
+    M, N, K = 384, 640, 512
+    wc.put(M, N, K, "fp16", k=3, choice={"key": HANDPICKED["medium"].key(), "us": 5.0, "family": "b200_sm100a_v1"},
+           extra={"torch_us": 100.0})
+    a, b = gate.make_inputs(M, N, K)
+    dispatch.enable(cache=wc)
+    try:
+        c = torch.matmul(a, b)
+        assert dispatch.stats()["routed"] == 1
+        assert gate.check_norm_relative(c, gate.reference(a, b), a, b).valid
+        x = a.clone().requires_grad_(True)
+        y = (x @ b).float().sum()
+        y.backward()
+        assert dispatch.stats()["routed"] == 2
+        assert torch.allclose(x.grad.float(), b.float().sum(1).expand(M, K), rtol=1e-2, atol=1e-1)
+        a2, b2 = gate.make_inputs(100, 100, 100)
+        torch.matmul(a2, b2)                          # no cache entry: torch
+        assert dispatch.stats()["torch"] >= 1
+    finally:
+        dispatch.disable()
+
+
+def test_torch_baseline_backend():
+    a, b = gate.make_inputs(64, 48, 32)
+    assert gate.validate(TorchMatmul(), 64, 48, 32, inputs=(a, b)).valid

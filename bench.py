@@ -40,9 +40,9 @@ METRIC = "fp16 GEMM TFLOP/s (% of B200 dense peak)"
 UNIT = "TFLOP/s"
 FALLBACK_PEAK_TFLOPS = 1590.0
 FLUSH_BYTES = 1 << 30
-# DRAM bytes (read + write) of one 16384^3 launch of the dominant kernel, scaled from an ncu capture of a smaller case;
-# see profiles/ for the capture and the scaling. None until measured.
-TRAFFIC_BYTES_16384 = None
+# DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of that exact launch
+# (profiles/gemm_16384_256x256x64_full.md): {(size, config key): bytes}. Other selections report null.
+TRAFFIC_BYTES = {(16384, "bm256_bn256_bk64_w4_s3_g8_sk1"): 6.764298e9 + 0.527529e9}
 
 
 def parse_args():
@@ -252,7 +252,7 @@ def main():
     peak, peak_src, _ = measured_peaks()
     dom = max(range(len(work)), key=lambda i: per_size_ms[i])
     achieved = work[dom]["flops"] / (per_size_ms[dom] / 1e3) / 1e12
-    traffic = TRAFFIC_BYTES_16384 if work[dom]["n"] == 16384 else None
+    traffic = TRAFFIC_BYTES.get((work[dom]["n"], work[dom]["cfg"].key()))
 
     # end to end through the public API: pinned host inputs copied in, matmul(), result copied back, every step
     e2e = None

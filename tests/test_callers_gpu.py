@@ -136,3 +136,13 @@ def test_dispatch_routes_a_cached_winner(tmp_path):
 def test_torch_baseline_backend():
     a, b = gate.make_inputs(64, 48, 32)
     assert gate.validate(TorchMatmul(), 64, 48, 32, inputs=(a, b)).valid
+
+
+def test_cublaslt_comparator_candidates_valid():
+    from cs464_b200 import cublaslt
+    for M, N, K in [(1, 4096, 4096), (129, 256, 1032), (512, 512, 512)]:
+        cs = cublaslt.candidates(M, N, K, n=8)
+        assert cs and cs[0].cfg["heuristic_rank"] == 0
+        a, b = gate.make_inputs(M, N, K)
+        for c in cs:
+            assert gate.validate(c, M, N, K, inputs=(a, b), norm_rel=True).valid, (M, N, K, c.key)

@@ -95,8 +95,10 @@ __device__ __forceinline__ Unit decode_unit(const KParams& p, int u) {
   const int r = t - gid * in_group;
   w.tm = first + r % gsz;
   w.tn = r / gsz;
-  w.kb0 = static_cast<int>(static_cast<int64_t>(w.split) * p.num_kb / p.split_k);
-  w.kb1 = static_cast<int>(static_cast<int64_t>(w.split + 1) * p.num_kb / p.split_k);
+  // (split + 1) * num_kb < 65 * 2^25 fits in 32 unsigned bits (num_kb <= 2^31 / 64, split_k <= 64)
+  const uint32_t nkb = static_cast<uint32_t>(p.num_kb), sk = static_cast<uint32_t>(p.split_k);
+  w.kb0 = static_cast<int>(static_cast<uint32_t>(w.split) * nkb / sk);
+  w.kb1 = static_cast<int>(static_cast<uint32_t>(w.split + 1) * nkb / sk);
   return w;
 }
 
@@ -211,7 +213,72 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
   const int first_unit = PAIR ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
   const int unit_step = PAIR ? static_cast<int>(num_clusters_x()) : static_cast<int>(gridDim.x);
 
+  // ---------------------------------------------------------------- TMA producer state (thread 0)
+  // The producer walks (unit, K block) pairs in order; `produce(n)` issues copies until n stages are in flight in
+  // total or the work runs out, so its first stages can go out before the block-wide barrier below.
+  int pu = first_unit - unit_step, pkb = 0, pkb1 = 0, prow_a = 0, prow_b = 0;
+  int ps = 0, pissued = 0;
+  uint32_t pph = 0;
+  bool pok = true;
+  const uint32_t tx_bytes = PAIR ? 2u * stage_bytes : stage_bytes;
+  auto produce = [&](int max_issue, uint32_t full_leader) {
+    while (pok && pissued < max_issue) {
+      while (pkb >= pkb1) {  // next unit with at least one K block
+        pu += unit_step;
+        if (pu >= p.units) return;
+        const Unit w = decode_unit(p, pu);
+        pkb = w.kb0;
+        pkb1 = w.kb1;
+        prow_a = w.tm * p.tile_m + static_cast<int>(rank) * p.cta_m;
+        prow_b = w.tn * p.tile_n + static_cast<int>(rank) * p.cta_n;
+      }
+      const uint32_t empty = ctl + OFF_EMPTY + 8 * ps;
+      if (!mbar_try_wait(empty, pph ^ 1u) &&
+          !wait_phase(empty, pph ^ 1u, abort_flag, p.status, p.timeout_ns, kStatusProducerTimeout)) {
+        pok = false;
+        return;
+      }
+      const uint32_t full = ctl + OFF_FULL + 8 * ps;
+      // the pair's leader counts both CTAs' bytes on its own barrier; the peer only issues copies
+      if (leader) mbar_arrive_expect_tx(full, tx_bytes);
+      const uint32_t full_c = full_leader + 8 * ps;
+      const uint32_t sa = data + ps * stage_bytes;
+      const uint32_t sb = sa + p.a_stage_bytes;
+      const int k0 = pkb * p.bk;
+      if (p.a_mn_major) {
+        for (int a = 0; a < p.cta_m / 64; ++a) {
+          if (PAIR) tma_load_2d_pair(sa + a * p.bk * 128, &tma_a, full_c, prow_a + a * 64, k0);
+          else tma_load_2d(sa + a * p.bk * 128, &tma_a, full, prow_a + a * 64, k0);
+        }
+      } else {
+        for (int a = 0; a < p.bk / 64; ++a) {
+          if (PAIR) tma_load_2d_pair(sa + a * p.cta_m * 128, &tma_a, full_c, k0 + a * 64, prow_a);
+          else tma_load_2d(sa + a * p.cta_m * 128, &tma_a, full, k0 + a * 64, prow_a);
+        }
+      }
+      if (p.b_mn_major) {
+        for (int a = 0; a < p.cta_n / 64; ++a) {
+          if (PAIR) tma_load_2d_pair(sb + a * p.bk * 128, &tma_b, full_c, prow_b + a * 64, k0);
+          else tma_load_2d(sb + a * p.bk * 128, &tma_b, full, prow_b + a * 64, k0);
+        }
+      } else {
+        for (int a = 0; a < p.bk / 64; ++a) {
+          if (PAIR) tma_load_2d_pair(sb + a * p.cta_n * 128, &tma_b, full_c, k0 + a * 64, prow_b);
+          else tma_load_2d(sb + a * p.cta_n * 128, &tma_b, full, k0 + a * 64, prow_b);
+        }
+      }
+      ++pissued;
+      ++pkb;
+      if (++ps == p.stages) {
+        ps = 0;
+        pph ^= 1u;
+      }
+    }
+  };
+
   if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(ctl + OFF_FULL + 8 * s, 1);
       mbar_init(ctl + OFF_EMPTY + 8 * s, 1);
@@ -223,8 +290,11 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     mbar_init(ctl + OFF_DRAIN, 1);
     *abort_flag = 0u;
     fence_mbar_init();
-    tma_prefetch_desc(&tma_a);
-    tma_prefetch_desc(&tma_b);
+    // A single CTA issues its first stage while warp 1 allocates tensor memory: only this thread has touched the
+    // barriers so far, and the other roles wait on them after the barrier below. One stage, not the whole ring:
+    // issuing more delays the barrier, and with it the first MMA. A pair's copies signal the leader's barriers,
+    // which exist only after the cluster barrier.
+    if (!PAIR) produce(1, ctl + OFF_FULL);
   }
   if (warp == 1) {
     if (PAIR) {
@@ -247,65 +317,13 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (every CTA loads its own tiles)
     if (lane == 0) {
-      int s = 0;
-      uint32_t ph = 0;
-      int issued = 0;
-      bool ok = true;
-      const uint32_t tx_bytes = PAIR ? 2u * stage_bytes : stage_bytes;
-      const uint32_t full_leader = PAIR ? map_to_rank(ctl + OFF_FULL, 0) : ctl + OFF_FULL;
-      for (int u = first_unit; u < p.units && ok; u += unit_step) {
-        const Unit w = decode_unit(p, u);
-        const int row_a = w.tm * p.tile_m + static_cast<int>(rank) * p.cta_m;
-        const int row_b = w.tn * p.tile_n + static_cast<int>(rank) * p.cta_n;
-        for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          const uint32_t empty = ctl + OFF_EMPTY + 8 * s;
-          if (!mbar_try_wait(empty, ph ^ 1u) &&
-              !wait_phase(empty, ph ^ 1u, abort_flag, p.status, p.timeout_ns, kStatusProducerTimeout)) {
-            ok = false;
-            break;
-          }
-          const uint32_t full = ctl + OFF_FULL + 8 * s;
-          // the pair's leader counts both CTAs' bytes on its own barrier; the peer only issues copies
-          if (leader) mbar_arrive_expect_tx(full, tx_bytes);
-          const uint32_t full_c = full_leader + 8 * s;
-          const uint32_t sa = data + s * stage_bytes;
-          const uint32_t sb = sa + p.a_stage_bytes;
-          const int k0 = kb * p.bk;
-          if (p.a_mn_major) {
-            for (int a = 0; a < p.cta_m / 64; ++a) {
-              if (PAIR) tma_load_2d_pair(sa + a * p.bk * 128, &tma_a, full_c, row_a + a * 64, k0);
-              else tma_load_2d(sa + a * p.bk * 128, &tma_a, full, row_a + a * 64, k0);
-            }
-          } else {
-            for (int a = 0; a < p.bk / 64; ++a) {
-              if (PAIR) tma_load_2d_pair(sa + a * p.cta_m * 128, &tma_a, full_c, k0 + a * 64, row_a);
-              else tma_load_2d(sa + a * p.cta_m * 128, &tma_a, full, k0 + a * 64, row_a);
-            }
-          }
-          if (p.b_mn_major) {
-            for (int a = 0; a < p.cta_n / 64; ++a) {
-              if (PAIR) tma_load_2d_pair(sb + a * p.bk * 128, &tma_b, full_c, row_b + a * 64, k0);
-              else tma_load_2d(sb + a * p.bk * 128, &tma_b, full, row_b + a * 64, k0);
-            }
-          } else {
-            for (int a = 0; a < p.bk / 64; ++a) {
-              if (PAIR) tma_load_2d_pair(sb + a * p.cta_n * 128, &tma_b, full_c, k0 + a * 64, row_b);
-              else tma_load_2d(sb + a * p.cta_n * 128, &tma_b, full, k0 + a * 64, row_b);
-            }
-          }
-          ++issued;
-          if (++s == p.stages) {
-            s = 0;
-            ph ^= 1u;
-          }
-        }
-      }
-      if (!ok && leader) {
+      produce(0x7fffffff, PAIR ? map_to_rank(ctl + OFF_FULL, 0) : ctl + OFF_FULL);
+      if (!pok && leader) {
         // Let the copies already issued land before shared memory is released (the leader's barriers count the
         // pair's bytes).
-        const int pending = min(issued, p.stages);
-        int ds = s;
-        uint32_t dph = ph;
+        const int pending = min(pissued, p.stages);
+        int ds = ps;
+        uint32_t dph = pph;
         for (int i = 0; i < pending; ++i) {
           if (--ds < 0) {
             ds = p.stages - 1;
@@ -429,9 +447,14 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
         tc_fence_after();
       }
       for (int h = 0; h < halves; ++h) {
-        const int64_t row =
-            static_cast<int64_t>(w.tm) * p.tile_m + static_cast<int64_t>(rank) * p.cta_m + h * 128 + q * 32 + lane;
+        // Rows and column chunks wholly outside C are skipped warp-uniformly (tcgen05.ld is warp-collective):
+        // a tile that overhangs the matrix edge costs only the part that exists.
+        const int64_t row0 =
+            static_cast<int64_t>(w.tm) * p.tile_m + static_cast<int64_t>(rank) * p.cta_m + h * 128 + q * 32;
+        if (row0 >= p.rows_a) break;
+        const int64_t row = row0 + lane;
         for (int c = grp; c < nchunks; c += kGroups) {
+          if (static_cast<int64_t>(w.tn) * p.tile_n + c * 32 >= p.rows_b) break;
           const int ncol = min(32, p.tile_n - c * 32);
           uint32_t v[32];
           if (zero) {

@@ -110,6 +110,7 @@ def search_one(shape: dict, *, k: int = 3, space: int | None = None, ranker=None
     chosen = choice.get("key")
     gap = (us[chosen] / scr["best_us"] - 1.0) if chosen in us and scr["best_us"] else None
     return {"M": M, "N": N, "K": K, "chosen": chosen, "chosen_short_us": choice.get("us"),
+            "screen": [[r["key"], round(r["us"], 3)] for r in scr["rows"] if r["status"] in ("ok", "slow")],
             "chosen_screen_us": us.get(chosen), "best_key": scr["best_key"], "best_us": scr["best_us"], "gap": gap,
             "n_screened": scr["n_configs"], "n_ok": sum(1 for r in scr["rows"] if r["status"] == "ok"),
             "select_s": t_select, "wall_s": time.perf_counter() - t0}

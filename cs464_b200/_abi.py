@@ -22,6 +22,7 @@ DTYPE_BF16 = 1
 
 SCHED_PERSISTENT = 0
 SCHED_TILE = 1
+SCHED_STREAMK = 2
 
 # every symbol include/b2g.h declares (checked by the CPU tests against the built library)
 EXPORTS = (

@@ -24,7 +24,7 @@ SPACE = {
     "num_stages": [2, 3, 4, 5, 6, 8],
     "GROUP_M": [1, 4, 8, 16],
     "SPLIT_K": [1, 2, 4, 8, 16],
-    "PERSISTENT": [1, 0],
+    "PERSISTENT": [1, 0, 2],              # 1 persistent tiles, 0 one CTA per tile, 2 stream-K
     "CLUSTER": [1, 2],                   # 2: CTA pair on two SMs, M = 256 tcgen05 MMAs
 }
 
@@ -102,6 +102,8 @@ def static_violations(cfg: MatmulConfig, hw: HwLimits, elem_bytes: int = 2) -> l
         reasons.append("cluster_half_n_not_multiple_of_64")
     if tmem_columns(cfg) > hw.tmem_columns:
         reasons.append("tmem_exceeds_limit")
+    if cfg.PERSISTENT == 2 and cfg.SPLIT_K != 1:
+        reasons.append("streamk_with_split_k")
     if cfg.num_warps == 8 and tn <= 32:
         # a second epilogue warpgroup would have no 32-column chunk of its own
         reasons.append("epilogue_warps_idle")

@@ -44,6 +44,7 @@ constexpr uint32_t kAlignSlack = 1024;  // data ring starts on the next 1024-byt
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s per wait: far above any legal stall
 constexpr uint64_t kDrainTimeoutNs = 50000000ull;   // 50 ms to drain in-flight work after an abort
 constexpr size_t kMaxSmemPerCta = 232448;          // sm_100 opt-in maximum dynamic shared memory per block
+constexpr int kDefaultSmCount = 148;                // B200, when no device is current (host-only sizing)
 
 // control block layout (byte offsets)
 constexpr uint32_t OFF_FULL = 0;      // kMaxStages x u64
@@ -53,11 +54,13 @@ constexpr uint32_t OFF_TEMPTY = 272;  // 2 x u64: accumulator drained by the epi
 constexpr uint32_t OFF_DRAIN = 288;   // u64: all MMAs of this CTA complete
 constexpr uint32_t OFF_TMEM = 296;    // u32: tensor-memory base address written by tcgen05.alloc
 constexpr uint32_t OFF_ABORT = 300;   // u32: set when any role gave up waiting
+constexpr uint32_t OFF_EPISYNC = 304; // u64: epilogue-warps rendezvous (stream-K fix-up), bounded like every wait
 
 // status codes written to the caller's device status word
 constexpr int kStatusProducerTimeout = 0x101;
 constexpr int kStatusMmaTimeout = 0x102;
 constexpr int kStatusEpilogueTimeout = 0x103;
+constexpr int kStatusStreamkTimeout = 0x104;
 
 enum OutKind : int32_t { OUT_F16 = 0, OUT_BF16 = 1, OUT_F32_PARTIAL = 2 };
 
@@ -78,28 +81,94 @@ struct KParams {
   int32_t out_kind, vec_ok;
   int* status;
   uint64_t timeout_ns;
+  // stream-K: workers (CTAs, or CTA pairs) share sk_iters = tiles * num_kb K blocks in equal contiguous slices; a tile
+  // split over several workers is finished by the worker holding its first K block (its owner), which adds the other
+  // workers' fp32 partials (one slot of cta_m x tile_n per CTA) in K order after their flags are raised.
+  int32_t streamk;
+  int32_t sk_dp_tiles;  // tiles 0 .. sk_dp_tiles-1 run whole, data-parallel (full waves)
+  int32_t sk_workers;   // workers 0 .. sk_workers-1 share the remaining tiles' K blocks
+  int64_t sk_iters;     // (tiles - sk_dp_tiles) * num_kb
+  float* sk_slots;
+  int* sk_flags;
 };
 
 struct Unit {
   int tm, tn, split, kb0, kb1;
+  int tile;  // tile index in the grouped order (stream-K)
 };
 
-__device__ __forceinline__ Unit decode_unit(const KParams& p, int u) {
-  Unit w;
-  const int t = u / p.split_k;
-  w.split = u - t * p.split_k;
+// (tm, tn) of the t-th tile in the grouped-M L2 order (kernels/triton_matmul.py:50-56)
+__device__ __forceinline__ void tile_coords(const KParams& p, int t, int& tm, int& tn) {
   const int in_group = p.group_m * p.tiles_n;
   const int gid = t / in_group;
   const int first = gid * p.group_m;
   const int gsz = min(p.tiles_m - first, p.group_m);
   const int r = t - gid * in_group;
-  w.tm = first + r % gsz;
-  w.tn = r / gsz;
+  tm = first + r % gsz;
+  tn = r / gsz;
+}
+
+__device__ __forceinline__ Unit decode_unit(const KParams& p, int u) {
+  Unit w;
+  const int t = u / p.split_k;
+  w.split = u - t * p.split_k;
+  w.tile = t;
+  tile_coords(p, t, w.tm, w.tn);
   // (split + 1) * num_kb < 65 * 2^25 fits in 32 unsigned bits (num_kb <= 2^31 / 64, split_k <= 64)
   const uint32_t nkb = static_cast<uint32_t>(p.num_kb), sk = static_cast<uint32_t>(p.split_k);
   w.kb0 = static_cast<int>(static_cast<uint32_t>(w.split) * nkb / sk);
   w.kb1 = static_cast<int>(static_cast<uint32_t>(w.split + 1) * nkb / sk);
   return w;
+}
+
+// First K-block iteration (global: tile * num_kb + kb) of stream-K worker `w`'s shared slice.
+__device__ __forceinline__ int64_t sk_start(const KParams& p, int64_t w) {
+  return static_cast<int64_t>(p.sk_dp_tiles) * p.num_kb + w * p.sk_iters / p.sk_workers;
+}
+
+// The sequence of work items of one worker: units worker, worker + workers, ... (tiles or split-K units). With
+// stream-K: first the worker's whole tiles of the data-parallel waves, then the (tile, K range) segments of its slice
+// of the shared K blocks. Every role walks the same sequence.
+struct Cursor {
+  int64_t it, hi;
+  int u;
+};
+
+__device__ __forceinline__ void cursor_init(const KParams& p, Cursor& c, int worker, int workers) {
+  (void)workers;
+  c.u = worker;
+  if (p.streamk) {
+    const bool shares = worker < p.sk_workers;
+    c.it = shares ? sk_start(p, worker) : 0;
+    c.hi = shares ? sk_start(p, worker + 1) : 0;
+  }
+}
+
+__device__ __forceinline__ bool cursor_next(const KParams& p, Cursor& c, int workers, Unit& w) {
+  if (p.streamk) {
+    if (c.u < p.sk_dp_tiles) {  // a whole tile of the data-parallel waves
+      w.tile = c.u;
+      w.split = 0;
+      w.kb0 = 0;
+      w.kb1 = p.num_kb;
+      tile_coords(p, w.tile, w.tm, w.tn);
+      c.u += workers;
+      return true;
+    }
+    if (c.it >= c.hi) return false;
+    const int64_t t = c.it / p.num_kb;
+    w.kb0 = static_cast<int>(c.it - t * p.num_kb);
+    w.kb1 = static_cast<int>(min(static_cast<int64_t>(p.num_kb), w.kb0 + (c.hi - c.it)));
+    w.tile = static_cast<int>(t);
+    w.split = 0;
+    tile_coords(p, w.tile, w.tm, w.tn);
+    c.it += w.kb1 - w.kb0;
+    return true;
+  }
+  if (c.u >= p.units) return false;
+  w = decode_unit(p, c.u);
+  c.u += workers;
+  return true;
 }
 
 // Bounded wait: true once the phase with `parity` completed; false if another role aborted or `timeout_ns` passed
@@ -130,6 +199,32 @@ __device__ __noinline__ void drain_phase(uint32_t bar, uint32_t parity, uint64_t
   while (!mbar_try_wait(bar, parity)) {
     if (global_timer_ns() - t0 > limit_ns) return;
   }
+}
+
+// ---- stream-K fix-up flags (global memory, one int per CTA slot)
+__device__ __forceinline__ int flag_acquire(const int* f) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void flag_release(int* f, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+
+// Bounded wait for a contributor's flag; false (and the stream-K status code) after timeout_ns.
+__device__ __noinline__ bool flag_wait(const int* f, volatile uint32_t* abort_flag, int* status, uint64_t timeout_ns) {
+  if (flag_acquire(f) == 1) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (flag_acquire(f) != 1) {
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > timeout_ns) {
+      *abort_flag = 1u;
+      if (status) atomicCAS(status, 0, kStatusStreamkTimeout);
+      return false;
+    }
+  }
+  return true;
 }
 
 __device__ __forceinline__ uint32_t cvt_pair(float a, float b, int bf16) {
@@ -216,7 +311,9 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
   // ---------------------------------------------------------------- TMA producer state (thread 0)
   // The producer walks (unit, K block) pairs in order; `produce(n)` issues copies until n stages are in flight in
   // total or the work runs out, so its first stages can go out before the block-wide barrier below.
-  int pu = first_unit - unit_step, pkb = 0, pkb1 = 0, prow_a = 0, prow_b = 0;
+  Cursor pc;
+  cursor_init(p, pc, first_unit, unit_step);
+  int pkb = 0, pkb1 = 0, prow_a = 0, prow_b = 0;
   int ps = 0, pissued = 0;
   uint32_t pph = 0;
   bool pok = true;
@@ -224,9 +321,8 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
   auto produce = [&](int max_issue, uint32_t full_leader) {
     while (pok && pissued < max_issue) {
       while (pkb >= pkb1) {  // next unit with at least one K block
-        pu += unit_step;
-        if (pu >= p.units) return;
-        const Unit w = decode_unit(p, pu);
+        Unit w;
+        if (!cursor_next(p, pc, unit_step, w)) return;
         pkb = w.kb0;
         pkb1 = w.kb1;
         prow_a = w.tm * p.tile_m + static_cast<int>(rank) * p.cta_m;
@@ -288,6 +384,7 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
       mbar_init(ctl + OFF_TEMPTY + 8 * b, (PAIR ? 2 : 1) * EPI_WARPS * 32);
     }
     mbar_init(ctl + OFF_DRAIN, 1);
+    mbar_init(ctl + OFF_EPISYNC, EPI_WARPS * 32);
     *abort_flag = 0u;
     fence_mbar_init();
     // A single CTA issues its first stage while warp 1 allocates tensor memory: only this thread has touched the
@@ -363,8 +460,10 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
       const uint32_t tfull0 = PAIR ? map_to_rank(ctl + OFF_TFULL, 0) : ctl + OFF_TFULL;
       const uint32_t tfull1 = PAIR ? map_to_rank(ctl + OFF_TFULL, 1) : 0u;
       const uint32_t idesc = p.idesc;
-      for (int u = first_unit; u < p.units && ok; u += unit_step) {
-        const Unit w = decode_unit(p, u);
+      Cursor mc;
+      cursor_init(p, mc, first_unit, unit_step);
+      Unit w;
+      while (ok && cursor_next(p, mc, unit_step, w)) {
         if (w.kb0 == w.kb1) continue;
         if (!mbar_try_wait(ctl + OFF_TEMPTY + 8 * acc, acc_ph ^ 1u) &&
             !wait_phase(ctl + OFF_TEMPTY + 8 * acc, acc_ph ^ 1u, abort_flag, p.status, p.timeout_ns,
@@ -437,14 +536,49 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     const int halves = PAIR ? 1 : p.tile_m / 128;
     const uint32_t tempty_leader = PAIR ? map_to_rank(ctl + OFF_TEMPTY, 0) : 0u;
     uint32_t acc = 0, acc_ph = 0;
-    for (int u = first_unit; u < p.units; u += unit_step) {
-      const Unit w = decode_unit(p, u);
+    const int epi_tid = static_cast<int>(threadIdx.x) - 64;
+    uint32_t sync_ph = 0;
+    // rendezvous of the epilogue warps through an mbarrier: bounded, so a thread that gave up cannot strand the rest
+    auto epilogue_sync = [&]() -> bool {
+      mbar_arrive(ctl + OFF_EPISYNC);
+      const bool ok = mbar_try_wait(ctl + OFF_EPISYNC, sync_ph) ||
+                      wait_phase(ctl + OFF_EPISYNC, sync_ph, abort_flag, p.status, p.timeout_ns, kStatusEpilogueTimeout);
+      sync_ph ^= 1u;
+      return ok;
+    };
+    const int64_t slot_elems = static_cast<int64_t>(p.cta_m) * p.tile_n;
+    float* const my_slot = p.streamk ? p.sk_slots + static_cast<int64_t>(blockIdx.x) * slot_elems : nullptr;
+    Cursor ec;
+    cursor_init(p, ec, first_unit, unit_step);
+    Unit w;
+    while (cursor_next(p, ec, unit_step, w)) {
       const bool zero = w.kb0 == w.kb1;
+      // stream-K: a segment covering only part of its tile either contributes a partial (it does not hold the
+      // tile's first K block) or owns the tile and adds the contributors' partials
+      const bool partial = p.streamk && !(w.kb0 == 0 && w.kb1 == p.num_kb);
+      const bool contrib = partial && w.kb0 > 0;
+      const bool owner = partial && w.kb0 == 0;
+      int j_end = first_unit + 1;  // contributors of an owned tile: workers first_unit + 1 .. j_end - 1
       if (!zero) {
         if (!wait_phase(ctl + OFF_TFULL + 8 * acc, acc_ph, abort_flag, p.status, p.timeout_ns,
                         kStatusEpilogueTimeout))
           break;
         tc_fence_after();
+      }
+      if (owner) {
+        const int64_t tile_end = static_cast<int64_t>(w.tile + 1) * p.num_kb;
+        while (j_end < p.sk_workers && sk_start(p, j_end) < tile_end) ++j_end;
+        // one thread polls the contributors' flags; the bounded rendezvous then orders every thread after its
+        // acquire loads
+        if (epi_tid == 0) {
+          for (int j = first_unit + 1; j < j_end; ++j) {
+            if (sk_start(p, j) == sk_start(p, j + 1)) continue;  // empty slice: no partial
+            if (!flag_wait(p.sk_flags + (PAIR ? 2 * j + static_cast<int>(rank) : j), abort_flag, p.status,
+                           p.timeout_ns))
+              break;
+          }
+        }
+        epilogue_sync();
       }
       for (int h = 0; h < halves; ++h) {
         // Rows and column chunks wholly outside C are skipped warp-uniformly (tcgen05.ld is warp-collective):
@@ -453,6 +587,7 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
             static_cast<int64_t>(w.tm) * p.tile_m + static_cast<int64_t>(rank) * p.cta_m + h * 128 + q * 32;
         if (row0 >= p.rows_a) break;
         const int64_t row = row0 + lane;
+        const int row_local = h * 128 + q * 32 + lane;  // row within this CTA's part of the tile
         for (int c = grp; c < nchunks; c += kGroups) {
           if (static_cast<int64_t>(w.tn) * p.tile_n + c * 32 >= p.rows_b) break;
           const int ncol = min(32, p.tile_n - c * 32);
@@ -470,8 +605,47 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
             }
             tmem_ld_wait();
           }
+          const int64_t slot_off = static_cast<int64_t>(row_local) * p.tile_n + c * 32;
+          if (contrib) {
+            float4* dst = reinterpret_cast<float4*>(my_slot + slot_off);
+#pragma unroll
+            for (int k4 = 0; k4 < 8; ++k4) {
+              if (k4 * 4 < ncol)
+                dst[k4] = make_float4(__uint_as_float(v[4 * k4]), __uint_as_float(v[4 * k4 + 1]),
+                                      __uint_as_float(v[4 * k4 + 2]), __uint_as_float(v[4 * k4 + 3]));
+            }
+            continue;
+          }
+          if (owner) {  // add the contributors' partials in K order (the hybrid schedule keeps them few)
+            for (int j = first_unit + 1; j < j_end; ++j) {
+              const float4* src = reinterpret_cast<const float4*>(
+                  p.sk_slots + static_cast<int64_t>(PAIR ? 2 * j + static_cast<int>(rank) : j) * slot_elems +
+                  slot_off);
+              float4 x[8];
+#pragma unroll
+              for (int k4 = 0; k4 < 8; ++k4)
+                if (k4 * 4 < ncol) x[k4] = src[k4];
+#pragma unroll
+              for (int k4 = 0; k4 < 8; ++k4) {
+                if (k4 * 4 < ncol) {
+                  v[4 * k4] = __float_as_uint(__uint_as_float(v[4 * k4]) + x[k4].x);
+                  v[4 * k4 + 1] = __float_as_uint(__uint_as_float(v[4 * k4 + 1]) + x[k4].y);
+                  v[4 * k4 + 2] = __float_as_uint(__uint_as_float(v[4 * k4 + 2]) + x[k4].z);
+                  v[4 * k4 + 3] = __float_as_uint(__uint_as_float(v[4 * k4 + 3]) + x[k4].w);
+                }
+              }
+            }
+          }
           store_chunk(p, w.split, row, static_cast<int64_t>(w.tn) * p.tile_n + c * 32, ncol, v);
         }
+      }
+      if (contrib) {  // publish the partial: every thread's stores, then one release of the flag
+        __threadfence();
+        if (epilogue_sync() && epi_tid == 0) flag_release(p.sk_flags + blockIdx.x, 1);
+      } else if (owner) {  // every partial has been read: lower the contributors' flags for the next launch
+        if (epilogue_sync() && epi_tid == 0)
+          for (int j = first_unit + 1; j < j_end; ++j)
+            flag_release(p.sk_flags + (PAIR ? 2 * j + static_cast<int>(rank) : j), 0);
       }
       if (!zero) {
         tc_fence_before();
@@ -651,6 +825,10 @@ struct Geometry {
   size_t smem;
   Operand a, b;  // MMA "A" (rows over tile_m) and MMA "B" (rows over tile_n)
   size_t ws_partial;  // split-K partial bytes
+  int streamk;
+  int64_t sk_iters;     // tiles * num_kb
+  int64_t sk_max_ctas;  // upper bound on resident CTAs (sizes the fix-up slots)
+  size_t sk_flags_off, sk_slots_off;
   size_t ws_total;
 };
 
@@ -701,8 +879,12 @@ int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g,
     return fail(B2G_ERR_UNSUPPORTED, "num_stages_invalid: stages must be in [2, 16]");
   if (cfg->group_m < 1) return fail(B2G_ERR_UNSUPPORTED, "group_m_invalid: GROUP_M must be >= 1");
   if (cfg->split_k < 1 || cfg->split_k > 64) return fail(B2G_ERR_UNSUPPORTED, "split_k_invalid: SPLIT_K in [1, 64]");
-  if (cfg->schedule != B2G_SCHED_PERSISTENT && cfg->schedule != B2G_SCHED_TILE)
+  if (cfg->schedule != B2G_SCHED_PERSISTENT && cfg->schedule != B2G_SCHED_TILE &&
+      cfg->schedule != B2G_SCHED_STREAMK)
     return fail(B2G_ERR_UNSUPPORTED, "schedule_invalid");
+  if (cfg->schedule == B2G_SCHED_STREAMK && cfg->split_k != 1)
+    return fail(B2G_ERR_UNSUPPORTED, "streamk_with_split_k: stream-K balances K itself; SPLIT_K must be 1");
+  g.streamk = cfg->schedule == B2G_SCHED_STREAMK;
   g.bk = bk;
   g.stages = cfg->num_stages;
   g.epi_warps = cfg->num_warps;
@@ -740,7 +922,29 @@ int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g,
   if (cfg->split_k > 1 && ws_elems >= (int64_t(1) << 40))
     return fail(B2G_ERR_UNSUPPORTED, "split_k_workspace_too_large");
   g.ws_partial = cfg->split_k > 1 ? static_cast<size_t>(round_up(ws_elems * 4, 256)) : 0;
-  g.a.ws_off = g.ws_partial;
+  size_t sk_bytes = 0;
+  g.sk_iters = static_cast<int64_t>(g.tiles_m) * g.tiles_n * g.num_kb;
+  g.sk_max_ctas = 0;
+  g.sk_flags_off = g.sk_slots_off = 0;
+  if (g.streamk) {
+    // at most as many resident CTAs as smem and tensor memory allow per SM on every SM
+    int sms = kDefaultSmCount;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+      int v = 0;
+      if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
+    } else {
+      cudaGetLastError();
+    }
+    const int64_t per_sm = std::max<int64_t>(
+        1, std::min<int64_t>(static_cast<int64_t>(kMaxSmemPerCta / g.smem), 512 / static_cast<int64_t>(g.tmem_cols)));
+    g.sk_max_ctas = static_cast<int64_t>(sms) * per_sm;
+    g.sk_flags_off = 0;  // flags first: the caller zeroes them once, the kernels leave them zero
+    g.sk_slots_off = static_cast<size_t>(round_up(g.sk_max_ctas * 4, 256));
+    sk_bytes = g.sk_slots_off +
+               static_cast<size_t>(round_up(g.sk_max_ctas * static_cast<int64_t>(g.cta_m) * g.tile_n * 4, 256));
+  }
+  g.a.ws_off = g.ws_partial + sk_bytes;
   g.b.ws_off = g.a.ws_off + packed_bytes(g.a);
   g.ws_total = g.b.ws_off + packed_bytes(g.b);
   return B2G_OK;
@@ -939,6 +1143,12 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
     k.tmem_cols = g.tmem_cols;
     k.status = status;
     k.timeout_ns = kWaitTimeoutNs;
+    k.streamk = g.streamk;
+    k.sk_dp_tiles = 0;
+    k.sk_workers = 1;
+    k.sk_iters = g.sk_iters;
+    k.sk_flags = g.streamk ? reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + g.sk_flags_off) : nullptr;
+    k.sk_slots = g.streamk ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + g.sk_slots_off) : nullptr;
     if (cfg->split_k > 1) {
       k.out = workspace;
       k.out_kind = OUT_F32_PARTIAL;
@@ -971,7 +1181,7 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
     p->smem = g.smem;
     // grid in work units (CTAs, or CTA pairs)
     int64_t grid = g.units;
-    if (cfg->schedule == B2G_SCHED_PERSISTENT) {
+    if (cfg->schedule == B2G_SCHED_PERSISTENT || cfg->schedule == B2G_SCHED_STREAMK) {
       int64_t slots = 0;
       if (g.pair) {
         cudaLaunchConfig_t lc = {};
@@ -1000,6 +1210,23 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
         slots = static_cast<int64_t>(sm_count) * occ;
       }
       grid = std::min<int64_t>(grid, slots);
+      if (g.streamk) {
+        // Every worker resident at once (owners wait for contributors). Whole waves of tiles run data-parallel; the
+        // last one or two waves' tiles are shared in K, by at most as many workers as keep a slice of
+        // max(4, num_kb / 4) K blocks each, so a tile is split a few ways, not per worker.
+        const int64_t tiles = static_cast<int64_t>(g.tiles_m) * g.tiles_n;
+        grid = std::min<int64_t>(slots, std::max<int64_t>(tiles, 1) * g.num_kb);
+        if (grid * (g.pair ? 2 : 1) > g.sk_max_ctas) grid = g.sk_max_ctas / (g.pair ? 2 : 1);
+        grid = std::max<int64_t>(grid, 1);
+        const int64_t dp_tiles = std::max<int64_t>(0, tiles / grid - 1) * grid;
+        const int64_t iters = (tiles - dp_tiles) * g.num_kb;
+        const int64_t min_slice = std::max<int64_t>(4, g.num_kb / 4);
+        const int64_t workers = std::max<int64_t>(1, std::min<int64_t>(grid, iters / min_slice));
+        p->kp.sk_dp_tiles = static_cast<int32_t>(dp_tiles);
+        p->kp.sk_iters = iters;
+        p->kp.sk_workers = static_cast<int32_t>(workers);
+        if (dp_tiles == 0) grid = workers;  // no data-parallel wave: idle workers need not launch
+      }
     }
     p->grid = static_cast<int>(std::max<int64_t>(grid, 1));
   }
@@ -1058,6 +1285,7 @@ const char* b2g_status_string(int32_t status) {
     case kStatusProducerTimeout: return "device wait timed out in the TMA producer";
     case kStatusMmaTimeout: return "device wait timed out in the MMA issuer";
     case kStatusEpilogueTimeout: return "device wait timed out in the epilogue";
+    case kStatusStreamkTimeout: return "stream-K owner timed out waiting for a contributor's partial";
     default: return "unknown device status";
   }
 }
@@ -1201,6 +1429,9 @@ int32_t b2g_gemm_noalloc(const b2g_config* cfg, const b2g_problem* prob, const v
   Geometry g;
   int32_t rc = make_geometry(cfg, prob, g, A, B);
   if (rc != B2G_OK) return rc;
+  if (g.streamk)
+    return fail(B2G_ERR_UNSUPPORTED,
+                "streamk_needs_workspace: stream-K fix-up flags must start zeroed in a caller workspace");
   if (g.a.pack || g.b.pack)
     return fail(B2G_ERR_UNSUPPORTED,
                 "operand_needs_staging: the allocation-free entry point reads A and B in place; it needs 16-byte "

@@ -35,7 +35,8 @@ class MatmulConfig:
     """One kernel variant. BLOCK_M x BLOCK_N output tile, BLOCK_K K step, num_warps epilogue warps (4 or 8),
     num_stages shared-memory ring depth, GROUP_M L2 tile grouping, SPLIT_K deterministic K splits. BLOCK_M <= 64 runs
     the operand-swapped skinny form. PERSISTENT=1: one CTA per SM slot walks the tiles; 0: one CTA per (tile, split),
-    the reference's grid (kernels/triton_matmul.py:99-100). CLUSTER=2: a pair of CTAs on two SMs computes each tile
+    the reference's grid (kernels/triton_matmul.py:99-100); 2: stream-K, persistent workers split tiles x K blocks
+    evenly and finish split tiles in K order (deterministic, needs SPLIT_K=1). CLUSTER=2: a pair of CTAs on two SMs computes each tile
     with M=256 tcgen05 MMAs (BLOCK_M = 256, or BLOCK_N = 256 in the skinny form), each CTA loading half of A and half
     of B."""
     BLOCK_M: int
@@ -69,7 +70,7 @@ class MatmulConfig:
         c = _abi.Config()
         c.block_m, c.block_n, c.block_k = self.BLOCK_M, self.BLOCK_N, self.BLOCK_K
         c.num_warps, c.num_stages, c.group_m, c.split_k = self.num_warps, self.num_stages, self.GROUP_M, self.SPLIT_K
-        c.schedule = _abi.SCHED_PERSISTENT if self.PERSISTENT else _abi.SCHED_TILE
+        c.schedule = {0: _abi.SCHED_TILE, 1: _abi.SCHED_PERSISTENT, 2: _abi.SCHED_STREAMK}[self.PERSISTENT]
         c.cluster = self.CLUSTER
         return c
 
@@ -179,7 +180,8 @@ class B200Matmul:
         with torch.cuda.device(dev):
             _abi.check(lib.b2g_workspace_size(ctypes.byref(acfg), ctypes.byref(pr), a.data_ptr(), b.data_ptr(),
                                               ctypes.byref(n)), "b2g_workspace_size")
-            ws = torch.empty(n.value, dtype=torch.uint8, device=dev) if n.value else None
+            # zeroed: the stream-K fix-up flags at its start must be 0 before the first launch
+            ws = torch.zeros(n.value, dtype=torch.uint8, device=dev) if n.value else None
             status = torch.zeros(1, dtype=torch.int32, device=dev)
             plan = ctypes.c_void_p()
             _abi.check(lib.b2g_plan_create(ctypes.byref(acfg), ctypes.byref(pr), a.data_ptr(), b.data_ptr(),
@@ -220,7 +222,7 @@ def gemm(cfg: MatmulConfig, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor 
     n = ctypes.c_size_t(0)
     _abi.check(lib.b2g_workspace_size(ctypes.byref(acfg), ctypes.byref(pr), a.data_ptr(), b.data_ptr(),
                                       ctypes.byref(n)), "b2g_workspace_size")
-    ws = torch.empty(n.value, dtype=torch.uint8, device=a.device) if n.value else None
+    ws = torch.zeros(n.value, dtype=torch.uint8, device=a.device) if n.value else None
     rc = lib.b2g_gemm(ctypes.byref(acfg), ctypes.byref(pr), a.data_ptr(), b.data_ptr(), c.data_ptr(),
                       ws.data_ptr() if ws is not None else None, n.value, status_word(a.device).data_ptr(),
                       torch.cuda.current_stream(a.device).cuda_stream)

@@ -62,9 +62,25 @@ def pruned_space(hw: HwLimits | None = None) -> list[MatmulConfig]:
     return _SPACE_CACHE[hw]
 
 
+SOFT_RULES = ("block_m_oversized", "block_n_oversized", "block_k_oversized", "group_m_noop")
+
+
 def shape_space(M: int, N: int, K: int, hw: HwLimits | None = None) -> list[MatmulConfig]:
-    """Every statically kept config with no shape-rule violation for (M, N, K)."""
-    return [c for c in pruned_space(hw) if not shape_violations(c, M, N, K)]
+    """Every statically kept config with no shape-rule violation for (M, N, K). When every config breaks a rule (a
+    dimension smaller than the smallest tile, e.g. N = 16), the tile-oversize rules are treated as soft: the configs
+    that break only those and overshoot the least are kept, so no shape is left without a candidate."""
+    pool = pruned_space(hw)
+    out = [c for c in pool if not shape_violations(c, M, N, K)]
+    if out:
+        return out
+    soft = [c for c in pool if all(r in SOFT_RULES for r in shape_violations(c, M, N, K))]
+    if not soft:
+        return []
+
+    def overshoot(c: MatmulConfig) -> tuple:
+        return (c.BLOCK_M / max(M, 1) + c.BLOCK_N / max(N, 1) + c.BLOCK_K / max(K, 1), c.key())
+    best = min(overshoot(c)[0] for c in soft)
+    return [c for c in soft if overshoot(c)[0] <= best * 1.5]
 
 
 def _ranker_default():

@@ -42,6 +42,10 @@ extern "C" {
 /* tile schedules */
 #define B2G_SCHED_PERSISTENT 0 /* one CTA per SM slot walks the tiles (default) */
 #define B2G_SCHED_TILE 1       /* one CTA per (tile, split): the reference's launch grid, kernels/triton_matmul.py:99-100 */
+#define B2G_SCHED_STREAMK 2    /* persistent workers share tiles x K blocks evenly; split tiles are finished in K order
+                                  by the worker holding their first K block. Needs SPLIT_K = 1 and a workspace whose
+                                  first bytes (the fix-up flags) are zero before the first launch; the kernels leave
+                                  them zero. After a device status error, zero the workspace again. */
 
 /*
  * One kernel variant. The first seven fields mean what MatmulConfig's fields mean (kernels/triton_matmul.py:20-28):

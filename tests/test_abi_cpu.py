@@ -51,6 +51,7 @@ def test_identity():
     (MatmulConfig(256, 256, 128, num_stages=4), (64, 64, 64), "smem_exceeds_limit"),
     (MatmulConfig(128, 128, 64, num_stages=1), (64, 64, 64), "num_stages_invalid"),
     (MatmulConfig(128, 128, 64, SPLIT_K=65), (64, 64, 64), "split_k_invalid"),
+    (MatmulConfig(128, 128, 64, SPLIT_K=2, PERSISTENT=2), (64, 64, 64), "streamk_with_split_k"),
 ])
 def test_check_rejects_with_named_rule(cfg, shape, reason):
     got = check_config(cfg, *shape)

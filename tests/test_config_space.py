@@ -47,7 +47,7 @@ def test_space_size_and_static_prune():
     n = 1
     for v in SPACE.values():
         n *= len(v)
-    assert len(space) == n == 38400
+    assert len(space) == n == 57600
     hw = HwLimits.b200()
     kept, dropped = prune(space, hw)
     assert 0 < len(kept) < len(space)

@@ -86,6 +86,24 @@ def test_split_k_uneven_k(split_k, bm):
     _assert_parity(c, oracle.gemm_f32(a, b), a, b, 1000)
 
 
+@pytest.mark.parametrize("cfg", [MatmulConfig(256, 256, 64, num_stages=3, PERSISTENT=2),
+                                 MatmulConfig(256, 256, 64, num_stages=6, CLUSTER=2, PERSISTENT=2),
+                                 MatmulConfig(16, 256, 64, num_stages=6, GROUP_M=1, PERSISTENT=2)],
+                         ids=lambda c: c.key())
+def test_stream_k_deterministic_and_correct(cfg):
+    """Few tiles, long K: every tile is split over several workers, so the owner fix-up does all the work; the
+    result must match the oracle and be bitwise identical run to run (fixed K-order sums, no atomics)."""
+    M, N, K = (1024, 1024, 8192) if cfg.BLOCK_M > 64 else (16, 2048, 16384)
+    a, b = oracle.make_inputs(M, N, K, seed=4)
+    run = B200Matmul(cfg).make_runner(a.cuda(), b.cuda())
+    c1 = run().clone()
+    c2 = run().clone()
+    torch.cuda.synchronize()
+    run.raise_on_status()
+    assert torch.equal(c1, c2)
+    _assert_parity(c1, oracle.reference_cpu(a, b).numpy(), a, b, K)
+
+
 def test_split_k_deterministic():
     cfg = MatmulConfig(128, 128, 64, SPLIT_K=8)
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -123,6 +141,12 @@ def test_bf16(name):
     MatmulConfig(256, 256, 64, num_stages=6, PERSISTENT=0, CLUSTER=2),
     MatmulConfig(32, 256, 128, num_stages=6, GROUP_M=1, CLUSTER=2),
     MatmulConfig(16, 256, 128, num_stages=6, GROUP_M=1, SPLIT_K=2, CLUSTER=2),
+    MatmulConfig(256, 256, 64, num_stages=3, PERSISTENT=2),
+    MatmulConfig(128, 128, 64, num_stages=6, PERSISTENT=2),
+    MatmulConfig(128, 256, 64, num_stages=4, num_warps=8, PERSISTENT=2),
+    MatmulConfig(256, 256, 64, num_stages=6, CLUSTER=2, PERSISTENT=2),
+    MatmulConfig(16, 256, 64, num_stages=6, GROUP_M=1, PERSISTENT=2),
+    MatmulConfig(32, 256, 128, num_stages=6, GROUP_M=1, CLUSTER=2, PERSISTENT=2),
 ], ids=lambda c: c.key())
 @pytest.mark.parametrize("shape", [(300, 520, 700), (1024, 1024, 1024), (40, 1000, 3000)])
 def test_knobs_match_oracle(cfg, shape):

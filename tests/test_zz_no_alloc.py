@@ -85,3 +85,6 @@ def test_noalloc_rejects_oversized_partials_and_staging():
     c_odd = torch.zeros(64, 64, device=dev, dtype=torch.float16)
     assert _noalloc(MatmulConfig(128, 128, 64), a_odd, b_odd, c_odd, status) == _abi.B2G_ERR_UNSUPPORTED
     assert "operand_needs_staging" in _abi.last_error()
+    # stream-K's fix-up flags need a zeroed workspace of the caller's
+    assert _noalloc(MatmulConfig(128, 128, 64, PERSISTENT=2), a, b, c, status) == _abi.B2G_ERR_UNSUPPORTED
+    assert "streamk" in _abi.last_error()

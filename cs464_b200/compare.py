@@ -18,7 +18,6 @@ import json
 import math
 import sys
 import time
-from pathlib import Path
 
 import torch
 
@@ -27,7 +26,6 @@ from cs464_b200.baselines import TorchMatmul
 from cs464_b200.gate import make_inputs, reference, validate
 from cs464_b200.keys import parse_key
 from cs464_b200.matmul import B200Matmul
-from cs464_b200.ranker import AnalyticRanker
 from cs464_b200.search import choose, measure, screen_shape, shape_space
 from cs464_b200.timing import TimingConfig, benchmark
 
@@ -48,7 +46,9 @@ def compare_shape(shape: dict, *, k: int = 3, space: int = 0, lt_n: int = 16, ra
     byts = 2.0 * (M * K + K * N + M * N)
     row = {"M": M, "N": N, "K": K, **{x: shape[x] for x in ("suite", "layer") if x in shape}}
     t0 = time.perf_counter()
-    ranker = ranker or AnalyticRanker()
+    if ranker is None:
+        from cs464_b200.search import _ranker_default
+        ranker = _ranker_default()
     keys = ranker.rank(M, N, K, k, order="diverse")
     sel = measure(M, N, K, dtype, [("b200_sm100a_v1", x, B200Matmul(parse_key(x))) for x in keys], inputs=(a, b, ref))
     choice = choose(sel["candidates"])

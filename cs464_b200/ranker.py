@@ -109,6 +109,81 @@ def candidate_features(M: int, N: int, K: int, cfg: MatmulConfig) -> dict:
 FEATURES = list(candidate_features(64, 64, 64, MatmulConfig(128, 128, 64)).keys())
 
 
+class _Pool:
+    """Per-config arrays of a pool, so a shape's features and analytic times are computed for all configs at once."""
+
+    def __init__(self, cfgs: list[MatmulConfig]):
+        self.cfgs = cfgs
+        f = lambda name: np.array([getattr(c, name) for c in cfgs], dtype=np.float64)  # noqa: E731
+        self.params = {name: f(name) for name in ("BLOCK_M", "BLOCK_N", "BLOCK_K", "num_warps", "num_stages",
+                                                   "GROUP_M", "SPLIT_K", "PERSISTENT", "CLUSTER")}
+        self.swapped = (self.params["BLOCK_M"] <= 64).astype(np.float64)
+        self.tm = np.where(self.swapped > 0, self.params["BLOCK_N"], self.params["BLOCK_M"])
+        self.tn = np.where(self.swapped > 0, self.params["BLOCK_M"], self.params["BLOCK_N"])
+        self.smem_kib = np.array([smem_bytes(c) for c in cfgs], dtype=np.float64) / 1024.0
+        self.spu = np.where(self.params["CLUSTER"] == 2, 2.0, 1.0)
+
+    def analytic_log_us(self, M: int, N: int, K: int) -> np.ndarray:
+        return np.log(self.analytic_s(M, N, K) * 1e6)
+
+    def geometry(self, M: int, N: int, K: int) -> dict:
+        P = self.params
+        rows_a = np.where(self.swapped > 0, N, M).astype(np.float64)
+        rows_b = np.where(self.swapped > 0, M, N).astype(np.float64)
+        tiles_m = np.ceil(rows_a / self.tm)
+        tiles_n = np.ceil(rows_b / self.tn)
+        nkb = np.maximum(1.0, np.ceil(K / P["BLOCK_K"]))
+        units = tiles_m * tiles_n * P["SPLIT_K"]
+        slots_all = np.floor(SM_COUNT / self.spu)
+        slots = np.where(P["PERSISTENT"] > 0, slots_all, units)
+        return {"rows_a": rows_a, "rows_b": rows_b, "tiles_m": tiles_m, "tiles_n": tiles_n, "nkb": nkb,
+                "kb_per_unit": np.ceil(nkb / P["SPLIT_K"]), "units": units, "slots": slots,
+                "waves": units / np.maximum(1.0, slots_all), "fill_m": rows_a / (tiles_m * self.tm),
+                "fill_n": rows_b / (tiles_n * self.tn)}
+
+    def analytic_s(self, M: int, N: int, K: int) -> np.ndarray:
+        """Vectorised `analytic_time_s` over the pool (same model, same constants)."""
+        P, g = self.params, self.geometry(M, N, K)
+        per_sm = PEAK_FLOPS / SM_COUNT / CLOCK_HZ
+        eff = np.maximum(np.minimum(1.0, self.tn / 64.0) ** 0.5, 0.25)
+        t_mma = 2.0 * self.tm * self.tn * P["BLOCK_K"] / self.spu / (per_sm * eff)
+        t_load = (self.tm + self.tn) * P["BLOCK_K"] * 2.0 / self.spu / L2_BYTES_PER_CLK_PER_SM
+        per_kb = np.maximum(t_mma, t_load) + KBLOCK_OVERHEAD_CLK
+        per_kb = per_kb + np.maximum(0.0, 2500.0 - P["num_stages"] * np.maximum(t_mma, t_load)) / P["num_stages"]
+        unit_clk = g["kb_per_unit"] * per_kb
+        acc_cols = np.where(P["CLUSTER"] == 2, self.tn, np.floor(self.tm / 128) * self.tn)
+        single = 2 * acc_cols > 512
+        epi = self.tm * self.tn * np.where(P["SPLIT_K"] == 1, 2.0, 4.0) / self.spu / (16.0 * P["num_warps"])
+        unit_clk = unit_clk + np.where(single, epi, 0.0)
+        workers = np.maximum(1.0, np.floor(SM_COUNT / self.spu))
+        iters = g["tiles_m"] * g["tiles_n"] * g["nkb"]
+        share = np.ceil(iters / np.minimum(workers, iters))
+        tpw = np.ceil(g["tiles_m"] * g["tiles_n"] / np.minimum(workers, iters))
+        t_sk = (share * per_kb + tpw * np.where(single, epi, 0.0)) / CLOCK_HZ + epi / CLOCK_HZ + STREAMK_FIXUP_S
+        waves = np.where(P["PERSISTENT"] > 0, np.ceil(g["units"] / np.maximum(1.0, g["slots"])), np.ceil(g["waves"]))
+        t_pt = waves * unit_clk / CLOCK_HZ + np.where(single, 0.0, epi / CLOCK_HZ)
+        t = np.where(P["PERSISTENT"] == 2, t_sk, t_pt)
+        dram = 2.0 * (M * K + K * N + M * N) + np.where(P["SPLIT_K"] > 1, 4.0 * P["SPLIT_K"] * M * N * 2 + 2.0 * M * N,
+                                                        0.0)
+        t = np.maximum(t, dram / HBM_BPS)
+        return (t + LAUNCH_S + np.where(P["SPLIT_K"] > 1, EXTRA_KERNEL_S, 0.0)
+                + np.where(P["CLUSTER"] == 2, CLUSTER_LAUNCH_S, 0.0))
+
+    def features(self, M: int, N: int, K: int) -> np.ndarray:
+        """The `candidate_features` matrix (rows = configs, columns = FEATURES)."""
+        g = self.geometry(M, N, K)
+        n = len(self.cfgs)
+        col = {"log2_M": np.full(n, math.log2(M)), "log2_N": np.full(n, math.log2(N)),
+               "log2_K": np.full(n, math.log2(K)), "log2_MNK": np.full(n, math.log2(M) + math.log2(N) + math.log2(K)),
+               **self.params, "swapped": self.swapped, "smem_kib": self.smem_kib, "fill_m": g["fill_m"],
+               "fill_n": g["fill_n"], "waves": g["waves"], "waves_frac": g["waves"] - np.floor(g["waves"]),
+               "log2_units": np.log2(g["units"]), "kb_per_unit": g["kb_per_unit"],
+               "log_analytic_us": self.analytic_log_us(M, N, K),
+               "log_dram_floor_us": np.full(n, math.log(2.0 * (M * K + K * N + M * N) / HBM_BPS * 1e6 + 1e-3)),
+               "log_tensor_floor_us": np.full(n, math.log(2.0 * M * N * K / PEAK_FLOPS * 1e6 + 1e-3))}
+        return np.stack([col[f] for f in FEATURES], axis=1)
+
+
 class AnalyticRanker:
     """Ranks the statically pruned space by the analytic time model (lower = better)."""
 
@@ -118,10 +193,13 @@ class AnalyticRanker:
         self.hw = hw or HwLimits.b200()
         self.cfgs = pool if pool is not None else prune(full_space(), self.hw)[0]
         self.pool_keys = [c.key() for c in self.cfgs]
+        self._pool = _Pool(self.cfgs) if self.cfgs else None
         self.stem = None
 
     def scores(self, M: int, N: int, K: int) -> np.ndarray:
-        return np.array([math.log(analytic_time_s(M, N, K, c)) for c in self.cfgs])
+        if self._pool is None:
+            return np.zeros(0)
+        return self._pool.analytic_log_us(M, N, K)
 
     def rank(self, M: int, N: int, K: int, k: int, order: str = "plain") -> list[str]:
         """Top-k keys among configs with no shape violation. "diverse" takes at most one config per tile
@@ -158,31 +236,30 @@ class LearnedRanker(AnalyticRanker):
         super().__init__(pool, hw)
         self.model = model
 
-    @staticmethod
-    def _matrix(M: int, N: int, K: int, cfgs: list[MatmulConfig]) -> np.ndarray:
-        return np.array([[candidate_features(M, N, K, c)[f] for f in FEATURES] for c in cfgs], dtype=np.float64)
-
     def fit(self, rows: list[dict], **kw) -> "LearnedRanker":
         """rows: {"M", "N", "K", "key", "us"} timings of valid candidates (several per shape)."""
         from sklearn.ensemble import HistGradientBoostingRegressor
 
         from cs464_b200.keys import parse_key
-        best: dict[tuple, float] = {}
+        by_shape: dict[tuple, list[dict]] = {}
         for r in rows:
-            s = (r["M"], r["N"], r["K"])
-            best[s] = min(best.get(s, math.inf), r["us"])
-        X = np.array([[candidate_features(r["M"], r["N"], r["K"], parse_key(r["key"]))[f] for f in FEATURES]
-                      for r in rows])
-        y = np.array([math.log(r["us"] / best[(r["M"], r["N"], r["K"])]) for r in rows])
+            by_shape.setdefault((r["M"], r["N"], r["K"]), []).append(r)
+        Xs, ys = [], []
+        for (M, N, K), rs in by_shape.items():
+            best = min(r["us"] for r in rs)
+            Xs.append(_Pool([parse_key(r["key"]) for r in rs]).features(M, N, K))
+            ys.append(np.log(np.array([r["us"] for r in rs]) / best))
+        X = np.concatenate(Xs)
+        y = np.concatenate(ys)
         params = {"max_iter": 400, "learning_rate": 0.06, "max_leaf_nodes": 48, "l2_regularization": 1e-3}
         params.update(kw)
         self.model = HistGradientBoostingRegressor(**params).fit(X, y)
         return self
 
     def scores(self, M: int, N: int, K: int) -> np.ndarray:
-        if self.model is None:
+        if self.model is None or self._pool is None:
             return super().scores(M, N, K)
-        return self.model.predict(self._matrix(M, N, K, self.cfgs))
+        return self.model.predict(self._pool.features(M, N, K))
 
     def save(self, stem: str | Path) -> None:
         import pickle
@@ -206,3 +283,54 @@ class LearnedRanker(AnalyticRanker):
         r = cls(model, [parse_key(k) for k in meta["pool"]])
         r.stem = str(stem)
         return r
+
+
+MODEL_STEM = Path(__file__).resolve().parent / "models" / "ranker_b200"
+
+
+def default_ranker():
+    """The shipped learned ranker when its files exist (cs464_b200/models/ranker_b200.{pkl,json}), else the analytic
+    one. A model whose feature list no longer matches this code is ignored (warned)."""
+    if Path(f"{MODEL_STEM}.pkl").exists() and Path(f"{MODEL_STEM}.json").exists():
+        try:
+            return LearnedRanker.load(MODEL_STEM)
+        except Exception as e:
+            import warnings
+            warnings.warn(f"learned ranker not usable ({type(e).__name__}: {e}); using the analytic ranker")
+    return AnalyticRanker()
+
+
+def rows_from_search(paths) -> list[dict]:
+    """Training rows {M, N, K, key, us} from sharded-search outputs (search_rank*.jsonl with screen rows)."""
+    from cs464_b200.keys import parse_key
+    out = []
+    for p in paths:
+        for line in Path(p).read_text().splitlines():
+            if not line.strip():
+                continue
+            r = json.loads(line)
+            for key, us in r.get("screen", []):
+                try:
+                    parse_key(key)
+                except ValueError:
+                    continue
+                if us and us > 0:
+                    out.append({"M": r["M"], "N": r["N"], "K": r["K"], "key": key, "us": float(us)})
+    return out
+
+
+def _main(argv=None) -> None:
+    import argparse
+    ap = argparse.ArgumentParser(description="train the learned ranker from sharded-search screens")
+    ap.add_argument("rows", nargs="+", help="search_rank*.jsonl files")
+    ap.add_argument("--out", default=str(MODEL_STEM))
+    ap.add_argument("--max-iter", type=int, default=400)
+    a = ap.parse_args(argv)
+    rows = rows_from_search(a.rows)
+    r = LearnedRanker().fit(rows, max_iter=a.max_iter)
+    r.save(a.out)
+    print(json.dumps({"rows": len(rows), "shapes": len({(x["M"], x["N"], x["K"]) for x in rows}), "out": a.out}))
+
+
+if __name__ == "__main__":
+    _main()

@@ -83,9 +83,15 @@ def shape_space(M: int, N: int, K: int, hw: HwLimits | None = None) -> list[Matm
     return [c for c in soft if overshoot(c)[0] <= best * 1.5]
 
 
+_DEFAULT_RANKER = None
+
+
 def _ranker_default():
-    from cs464_b200.ranker import AnalyticRanker
-    return AnalyticRanker()
+    global _DEFAULT_RANKER
+    if _DEFAULT_RANKER is None:
+        from cs464_b200.ranker import default_ranker
+        _DEFAULT_RANKER = default_ranker()
+    return _DEFAULT_RANKER
 
 
 def candidates_for(spec: str, M: int, N: int, K: int, prune_shapes: bool = False, ranker=None) -> list[Candidate]:

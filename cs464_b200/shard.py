@@ -88,12 +88,13 @@ def search_one(shape: dict, *, k: int = 3, space: int | None = None, ranker=None
     from cs464_b200.keys import parse_key
     from cs464_b200.search import choose, measure, screen_shape, shape_space
     from cs464_b200.matmul import B200Matmul
-    from cs464_b200.ranker import AnalyticRanker
     M, N, K = shape["M"], shape["N"], shape["K"]
     t0 = time.perf_counter()
     a, b = make_inputs(M, N, K, torch.float16, scale_b=shape.get("weight_std", 1.0))
     ref = reference(a, b)
-    ranker = ranker or AnalyticRanker()
+    if ranker is None:
+        from cs464_b200.search import _ranker_default
+        ranker = _ranker_default()
     keys = ranker.rank(M, N, K, k, order="diverse")
     sel = measure(M, N, K, torch.float16, [("b200_sm100a_v1", key, B200Matmul(parse_key(key))) for key in keys],
                   inputs=(a, b, ref))

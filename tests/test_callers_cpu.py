@@ -240,3 +240,27 @@ def test_suites():
                                                                  (14336, 4096)}
     for name in suites.SUITES:
         assert suites.load(name) == json.loads((suites.DATA / f"{name}.json").read_text())["shapes"]
+
+
+def test_vectorised_pool_matches_scalar_model():
+    from cs464_b200.ranker import FEATURES, _Pool
+    pool = shape_space(777, 1234, 2048)[::53]
+    P = _Pool(pool)
+    for shape in [(777, 1234, 2048), (1, 28672, 4096), (8192, 8192, 8192), (40, 160, 2376)]:
+        vec = P.analytic_s(*shape)
+        ref = np.array([analytic_time_s(*shape, c) for c in pool])
+        assert np.allclose(vec, ref, rtol=1e-9), shape
+        F = P.features(*shape)
+        ref_f = np.array([[candidate_features(*shape, c)[f] for f in FEATURES] for c in pool])
+        assert np.allclose(F, ref_f, rtol=1e-9, atol=1e-12), shape
+
+
+def test_ranker_training_rows_and_default(tmp_path):
+    from cs464_b200 import ranker as rk
+    row = {"M": 64, "N": 128, "K": 256, "screen": [["bm128_bn128_bk64_w4_s6_g8_sk1", 5.0], ["bad_key", 1.0],
+                                                   ["bm16_bn128_bk128_w4_s6_g1_sk1", 4.0]]}
+    p = tmp_path / "search_rank0.jsonl"
+    p.write_text(json.dumps(row) + "\n")
+    rows = rk.rows_from_search([p])
+    assert len(rows) == 2 and {r["key"] for r in rows} == {"bm128_bn128_bk64_w4_s6_g8_sk1", "bm16_bn128_bk128_w4_s6_g1_sk1"}
+    assert hasattr(rk.default_ranker(), "rank")

@@ -432,7 +432,9 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (the pair's leader issues for both)
-    if (lane == 0 && leader) {
+    // The whole warp walks the loop and waits together; lane 0 alone issues the MMAs and commits (predicated), so
+    // the warp stays converged and the descriptors uniform.
+    if (leader) {
       int s = 0;
       uint32_t ph = 0;
       uint32_t acc = 0, acc_ph = 0;
@@ -491,18 +493,18 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
               const uint64_t bd = b_s + ((kk >> 2) * b_step4 + (kk & 3) * b_step1);
               const uint32_t accumulate = kk == 0 ? first : 1u;
               if (PAIR) {
-                umma_f16_pair(d_base, ad, bd, idesc, accumulate);
+                umma_f16_pair_w(d_base, ad, bd, idesc, accumulate);
               } else {
-                umma_f16(d_base, ad, bd, idesc, accumulate);
-                if (two_halves) umma_f16(d_base + p.tile_n, ad + a_half16, bd, idesc, accumulate);
+                umma_f16_w(d_base, ad, bd, idesc, accumulate);
+                if (two_halves) umma_f16_w(d_base + p.tile_n, ad + a_half16, bd, idesc, accumulate);
               }
             }
           }
           if (PAIR) {
-            umma_commit_pair(empty0 + 8 * s);
-            umma_commit_pair(empty1 + 8 * s);
+            umma_commit_pair_w(empty0 + 8 * s);
+            umma_commit_pair_w(empty1 + 8 * s);
           } else {
-            umma_commit(empty0 + 8 * s);
+            umma_commit_w(empty0 + 8 * s);
           }
           if (++s == p.stages) {
             s = 0;
@@ -511,10 +513,10 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
         }
         if (!ok) break;
         if (PAIR) {
-          umma_commit_pair(tfull0 + 8 * acc);
-          umma_commit_pair(tfull1 + 8 * acc);
+          umma_commit_pair_w(tfull0 + 8 * acc);
+          umma_commit_pair_w(tfull1 + 8 * acc);
         } else {
-          umma_commit(tfull0 + 8 * acc);
+          umma_commit_w(tfull0 + 8 * acc);
         }
         if (++acc == p.num_acc) {
           acc = 0;
@@ -522,8 +524,8 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
         }
       }
       // Every MMA this thread issued has finished before tensor memory is released.
-      if (PAIR) umma_commit_pair(map_to_rank(ctl + OFF_DRAIN, 0));
-      else umma_commit(ctl + OFF_DRAIN);
+      if (PAIR) umma_commit_pair_w(map_to_rank(ctl + OFF_DRAIN, 0));
+      else umma_commit_w(ctl + OFF_DRAIN);
       drain_phase(ctl + OFF_DRAIN, 0, ok ? kWaitTimeoutNs : kDrainTimeoutNs);
     }
   } else {

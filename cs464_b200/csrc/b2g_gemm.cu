@@ -73,6 +73,7 @@ struct KParams {
   int32_t group_m, split_k;
   int32_t tiles_m, tiles_n, num_kb, units;
   int32_t a_mn_major, b_mn_major;
+  int32_t a_3d, b_3d;  // MN-major operand read by one 3-D copy per K block (all its 64-wide column groups)
   uint32_t idesc;
   uint32_t a_stage_bytes, b_stage_bytes;
   uint32_t acc_cols, num_acc, tmem_cols;
@@ -341,7 +342,10 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
       const uint32_t sa = data + ps * stage_bytes;
       const uint32_t sb = sa + p.a_stage_bytes;
       const int k0 = pkb * p.bk;
-      if (p.a_mn_major) {
+      if (p.a_3d) {
+        if (PAIR) tma_load_3d_pair(sa, &tma_a, full_c, 0, k0, prow_a / 64);
+        else tma_load_3d(sa, &tma_a, full, 0, k0, prow_a / 64);
+      } else if (p.a_mn_major) {
         for (int a = 0; a < p.cta_m / 64; ++a) {
           if (PAIR) tma_load_2d_pair(sa + a * p.bk * 128, &tma_a, full_c, prow_a + a * 64, k0);
           else tma_load_2d(sa + a * p.bk * 128, &tma_a, full, prow_a + a * 64, k0);
@@ -352,7 +356,10 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
           else tma_load_2d(sa + a * p.cta_m * 128, &tma_a, full, k0 + a * 64, prow_a);
         }
       }
-      if (p.b_mn_major) {
+      if (p.b_3d) {
+        if (PAIR) tma_load_3d_pair(sb, &tma_b, full_c, 0, k0, prow_b / 64);
+        else tma_load_3d(sb, &tma_b, full, 0, k0, prow_b / 64);
+      } else if (p.b_mn_major) {
         for (int a = 0; a < p.cta_n / 64; ++a) {
           if (PAIR) tma_load_2d_pair(sb + a * p.bk * 128, &tma_b, full_c, prow_b + a * 64, k0);
           else tma_load_2d(sb + a * p.bk * 128, &tma_b, full, prow_b + a * 64, k0);
@@ -977,11 +984,27 @@ int32_t init_device(int dev, int& sm_count) {
   return B2G_OK;
 }
 
-int32_t encode_operand(const Operand& o, const void* base, int dtype, int bk, CUtensorMap* map) {
+int32_t encode_operand(const Operand& o, const void* base, int dtype, int bk, CUtensorMap* map, int32_t* is3d) {
   std::string err;
   EncodeTiledFn enc = get_encode_fn(err);
   if (!enc) return fail(B2G_ERR_CUDA, err);
   const CUtensorMapDataType dt = dtype == B2G_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  *is3d = 0;
+  // An MN-major operand whose rows are whole 64-wide groups is described as (64 rows, K, row groups), so one copy
+  // per K block fetches every group a CTA needs. The groups never reach past the last row, so nothing outside the
+  // matrix is read. If the driver declines the shape, the 2-D description below is used.
+  if (o.mn_major && o.tile_rows > 64 && o.tile_rows % 64 == 0 && o.rows % 64 == 0) {
+    cuuint64_t dims3[3] = {64, static_cast<cuuint64_t>(o.K), static_cast<cuuint64_t>(o.rows / 64)};
+    cuuint64_t strides3[2] = {static_cast<cuuint64_t>(o.ld) * 2, 128};
+    cuuint32_t box3[3] = {64, static_cast<cuuint32_t>(bk), static_cast<cuuint32_t>(o.tile_rows / 64)};
+    cuuint32_t estr3[3] = {1, 1, 1};
+    if (enc(map, dt, 3, const_cast<void*>(base), dims3, strides3, box3, estr3, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+      *is3d = 1;
+      return B2G_OK;
+    }
+  }
   cuuint64_t dims[2];
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(o.ld) * 2};
   cuuint32_t box[2];
@@ -1115,10 +1138,10 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
       fill_pack(g.b, workspace, p->pb_src, p->pb_so, p->pb_si, p->pb_ld, p->pb_outer, p->pb_inner, p->pb_dst);
       b_base = p->pb_dst;
     }
-    rc = encode_operand(g.a, a_base, prob->dtype, g.bk, &p->tma_a);
-    if (rc == B2G_OK) rc = encode_operand(g.b, b_base, prob->dtype, g.bk, &p->tma_b);
-    if (rc != B2G_OK) return rc;
     KParams& k = p->kp;
+    rc = encode_operand(g.a, a_base, prob->dtype, g.bk, &p->tma_a, &k.a_3d);
+    if (rc == B2G_OK) rc = encode_operand(g.b, b_base, prob->dtype, g.bk, &p->tma_b, &k.b_3d);
+    if (rc != B2G_OK) return rc;
     k.rows_a = static_cast<int32_t>(g.swapped ? N : M);
     k.rows_b = static_cast<int32_t>(g.swapped ? M : N);
     k.K = static_cast<int32_t>(K);

@@ -64,6 +64,25 @@ constexpr int kStatusStreamkTimeout = 0x104;
 
 enum OutKind : int32_t { OUT_F16 = 0, OUT_BF16 = 1, OUT_F32_PARTIAL = 2 };
 
+// n / d for 0 <= n < 2^31 by a multiply-high and a shift (round-up reciprocal, Granlund & Montgomery 1994): the
+// tile decode runs on one thread per role, where a chain of hardware-less 32-bit divisions costs hundreds of cycles.
+struct FastDiv {
+  uint32_t d, m, s;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f;
+  f.d = d < 1 ? 1 : d;
+  f.s = 0;
+  while ((uint64_t(1) << f.s) < f.d) ++f.s;
+  f.m = static_cast<uint32_t>(((uint64_t(1) << 32) * ((uint64_t(1) << f.s) - f.d)) / f.d + 1);
+  return f;
+}
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+  return static_cast<uint32_t>((static_cast<uint64_t>(__umulhi(n, f.m)) + n) >> f.s);
+}
+
 // Kernel parameters, in the MMA's orientation: D[i, j] with i over `rows_a` (tensor-memory lanes) and j over
 // `rows_b` (tensor-memory columns). Without the swap i = m, j = n; with it i = n, j = m.
 struct KParams {
@@ -72,6 +91,9 @@ struct KParams {
   int32_t cta_m, cta_n;  // A and B rows one CTA loads (tile_m, tile_n; halves of them in a CTA pair)
   int32_t group_m, split_k;
   int32_t tiles_m, tiles_n, num_kb, units;
+  // divisors of the tile decode: split_k, group_m * tiles_n, group_m, and the last group's height
+  FastDiv fd_split, fd_group, fd_gm, fd_last;
+  int32_t last_group_first;  // first tile row of the last (possibly shorter) group
   int32_t a_mn_major, b_mn_major;
   int32_t a_3d, b_3d;  // MN-major operand read by one 3-D copy per K block (all its 64-wide column groups)
   uint32_t idesc;
@@ -100,25 +122,32 @@ struct Unit {
 
 // (tm, tn) of the t-th tile in the grouped-M L2 order (kernels/triton_matmul.py:50-56)
 __device__ __forceinline__ void tile_coords(const KParams& p, int t, int& tm, int& tn) {
-  const int in_group = p.group_m * p.tiles_n;
-  const int gid = t / in_group;
-  const int first = gid * p.group_m;
-  const int gsz = min(p.tiles_m - first, p.group_m);
-  const int r = t - gid * in_group;
-  tm = first + r % gsz;
-  tn = r / gsz;
+  const uint32_t gid = fdiv(static_cast<uint32_t>(t), p.fd_group);
+  const int first = static_cast<int>(gid) * p.group_m;
+  const int r = t - static_cast<int>(gid) * p.group_m * p.tiles_n;
+  const FastDiv& g = first == p.last_group_first ? p.fd_last : p.fd_gm;
+  const int q = static_cast<int>(fdiv(static_cast<uint32_t>(r), g));
+  tm = first + (r - q * static_cast<int>(g.d));
+  tn = q;
 }
 
 __device__ __forceinline__ Unit decode_unit(const KParams& p, int u) {
   Unit w;
-  const int t = u / p.split_k;
-  w.split = u - t * p.split_k;
-  w.tile = t;
-  tile_coords(p, t, w.tm, w.tn);
-  // (split + 1) * num_kb < 65 * 2^25 fits in 32 unsigned bits (num_kb <= 2^31 / 64, split_k <= 64)
-  const uint32_t nkb = static_cast<uint32_t>(p.num_kb), sk = static_cast<uint32_t>(p.split_k);
-  w.kb0 = static_cast<int>(static_cast<uint32_t>(w.split) * nkb / sk);
-  w.kb1 = static_cast<int>(static_cast<uint32_t>(w.split + 1) * nkb / sk);
+  if (p.split_k == 1) {
+    w.split = 0;
+    w.tile = u;
+    w.kb0 = 0;
+    w.kb1 = p.num_kb;
+  } else {
+    const int t = static_cast<int>(fdiv(static_cast<uint32_t>(u), p.fd_split));
+    w.split = u - t * p.split_k;
+    w.tile = t;
+    // split * num_kb / split_k: below 2^31 because split_k * num_kb is (checked when the plan is made)
+    const uint32_t nkb = static_cast<uint32_t>(p.num_kb);
+    w.kb0 = static_cast<int>(fdiv(static_cast<uint32_t>(w.split) * nkb, p.fd_split));
+    w.kb1 = static_cast<int>(fdiv(static_cast<uint32_t>(w.split + 1) * nkb, p.fd_split));
+  }
+  tile_coords(p, w.tile, w.tm, w.tn);
   return w;
 }
 
@@ -409,6 +438,9 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
       tmem_relinquish();
     }
   }
+  // Lane 0 of warp 0 may still be issuing its first copies: the warp converges first, because a block or cluster
+  // barrier reached by part of a warp counts the whole warp as arrived.
+  __syncwarp();
   tc_fence_before();
   if (PAIR) {
     cluster_sync();  // both CTAs' barriers initialised and tensor memory allocated before any cross-CTA signal
@@ -919,6 +951,8 @@ int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g,
   g.num_kb = static_cast<int>((K + bk - 1) / bk);
   const int64_t units = static_cast<int64_t>(g.tiles_m) * g.tiles_n * cfg->split_k;
   if (units >= (int64_t(1) << 31)) return fail(B2G_ERR_UNSUPPORTED, "too_many_tiles");
+  if (static_cast<int64_t>(cfg->split_k) * g.num_kb >= (int64_t(1) << 31))
+    return fail(B2G_ERR_UNSUPPORTED, "split_k_too_deep: SPLIT_K x K blocks must be < 2^31");
   g.units = static_cast<int>(units);
   // fp32 accumulator columns per CTA: a pair's CTA holds its 128 rows x tile_n
   g.acc_cols = static_cast<uint32_t>(g.pair ? g.tile_n : g.tile_m / 128 * g.tile_n);
@@ -1151,8 +1185,18 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
     k.cta_n = g.cta_n;
     k.bk = g.bk;
     k.stages = g.stages;
-    k.group_m = cfg->group_m;
+    // a group taller than the matrix is one group of all tile rows: same order, and the divisors stay small
+    k.group_m = std::max(1, std::min(cfg->group_m, g.tiles_m));
     k.split_k = cfg->split_k;
+    {
+      const int gm = k.group_m;
+      const int last_first = ((g.tiles_m - 1) / gm) * gm;
+      k.fd_split = make_fastdiv(static_cast<uint32_t>(std::max(1, cfg->split_k)));
+      k.fd_group = make_fastdiv(static_cast<uint32_t>(gm) * static_cast<uint32_t>(g.tiles_n));
+      k.fd_gm = make_fastdiv(static_cast<uint32_t>(gm));
+      k.fd_last = make_fastdiv(static_cast<uint32_t>(std::min(gm, g.tiles_m - last_first)));
+      k.last_group_first = last_first;
+    }
     k.tiles_m = g.tiles_m;
     k.tiles_n = g.tiles_n;
     k.num_kb = g.num_kb;

@@ -107,3 +107,30 @@ def test_plan_create_without_gpu_reports_cuda_error():
                              None, 0, None, ctypes.byref(plan))
     assert rc == _abi.B2G_ERR_CUDA
     assert plan.value is None
+
+
+def test_fast_division_method_used_by_the_tile_decode():
+    """The kernel divides tile and split indices by a multiply-high and a shift (round-up reciprocal): m =
+    floor(2^32 * (2^s - d) / d) + 1 with s = ceil(log2 d), q = (umulhi(n, m) + n) >> s, for 0 <= n < 2^31. This
+    restates the host set-up (`make_fastdiv`) and the device step (`fdiv`) and checks them against exact division."""
+    import random
+
+    def make(d):
+        s = 0
+        while (1 << s) < d:
+            s += 1
+        return ((1 << 32) * ((1 << s) - d)) // d + 1, s
+
+    def fdiv(n, m, s):
+        return (((n * m) >> 32) + n) >> s
+
+    rng = random.Random(0)
+    divisors = [1, 2, 3, 5, 7, 8, 13, 16, 64, 127, 148, 1000, 4096, (1 << 20) + 3, (1 << 30) - 1, (1 << 31) - 1]
+    divisors += [rng.randrange(1, 1 << 31) for _ in range(40)]
+    for d in divisors:
+        m, s = make(d)
+        assert 0 < m < (1 << 32) or d == 1
+        ns = [0, 1, d - 1, d, d + 1, 2 * d - 1, (1 << 31) - 1, (1 << 31) - 2] + [rng.randrange(0, 1 << 31) for _ in range(300)]
+        for n in ns:
+            if 0 <= n < (1 << 31):
+                assert fdiv(n, m, s) == n // d, (n, d)

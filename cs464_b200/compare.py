@@ -1,6 +1,6 @@
 """Per-shape comparison of the sm_100a family with cuBLASLt and torch.matmul (BASELINE configs 3 and 4).
 
-For every shape of a suite, on one GPU, with one timing protocol (cold L2, CUDA events, median):
+For every shape of a suite, on one GPU, with one timing protocol (cold L2, CUDA events, trimmed mean of the samples):
   * `sel`   the family's zero-search pick: the ranker's top-k validated and short-timed, the fastest kept
             (`search.search_shape` + `choose`), then re-timed with the full protocol;
   * `best`  the family's best-in-pool over a screen of the shape-pruned space (`--space N` configs, 0 = skip);
@@ -34,7 +34,7 @@ FULL = TimingConfig(cache_mode="cold", warmup_ms=5.0, min_warmup_iters=2, min_re
 
 
 def _time(backend, a, b) -> float:
-    return benchmark(backend.make_runner(a, b), FULL).median_us
+    return benchmark(backend.make_runner(a, b), FULL).trimmed_mean_us
 
 
 def compare_shape(shape: dict, *, k: int = 3, space: int = 0, lt_n: int = 16, ranker=None) -> dict:

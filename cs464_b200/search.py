@@ -28,7 +28,7 @@ from cs464_b200.timing import SMALL_US, TimingConfig, benchmark, short_configs
 FAMILY = B200Matmul.family
 DTYPE_NAMES = {torch.float16: "fp16", torch.bfloat16: "bf16"}
 SLOW_FACTOR = 1.5
-SCREEN_SAMPLES = 5
+SCREEN_SAMPLES = 15
 
 
 @dataclass
@@ -247,7 +247,9 @@ def screen_shape(M: int, N: int, K: int, configs: list[MatmulConfig] | None = No
                  slow_factor: float = SLOW_FACTOR, samples: int = SCREEN_SAMPLES, inputs=None,
                  log=None) -> dict:
     """Time every config (default: the shape-pruned space) with early cut-off. Each config: validate; one cold sample
-    (its median of `1` after warm-up); cut as "slow" if above slow_factor x the best so far; else `samples` cold samples.
+    (its median of `1` after warm-up); cut as "slow" if above slow_factor x the best so far; else `samples` cold samples,
+    summarised by their trimmed mean: per-launch event timestamps on this GPU fall on a ~1 us grid, so the median of a
+    few samples of a 10 us kernel moves in 10 % steps, while the mean of the middle samples resolves finer.
     Returns {"rows": [{key, status, us, n}], "best_key", "best_us", "n_configs", "wall_s"}."""
     t0 = time.perf_counter()
     cfgs = configs if configs is not None else shape_space(M, N, K)
@@ -274,7 +276,7 @@ def screen_shape(M: int, N: int, K: int, configs: list[MatmulConfig] | None = No
         if us > slow_factor * best:
             rows.append({"key": c.key(), "status": "slow", "us": us, "n": 1})
             continue
-        us = benchmark(run, more).median_us
+        us = benchmark(run, more).trimmed_mean_us
         best = min(best, us)
         rows.append({"key": c.key(), "status": "ok", "us": us, "n": samples})
         if log:

@@ -59,6 +59,7 @@ class TimingResult:
     p75_us: float
     p90_us: float
     p99_us: float
+    trimmed_mean_us: float  # mean of the middle 60 % of samples: finer than the median when samples are quantised
     n_samples: int
     rse: float
     converged: bool
@@ -88,9 +89,13 @@ def summarize(samples_us, *, rse_target: float = 0.01) -> dict:
     std = float(s.std(ddof=1)) if n > 1 else 0.0
     rse = std / math.sqrt(n) / mean if n > 1 and mean > 0 else math.inf
     q = np.percentile(s, [10, 25, 50, 75, 90, 99])
+    srt = np.sort(s)
+    cut = int(0.2 * n)
+    mid = srt[cut:n - cut] if n - 2 * cut > 0 else srt
     return {"median_us": float(q[2]), "mean_us": mean, "std_us": std, "min_us": float(s.min()), "max_us": float(s.max()),
             "p10_us": float(q[0]), "p25_us": float(q[1]), "p75_us": float(q[3]), "p90_us": float(q[4]),
-            "p99_us": float(q[5]), "n_samples": n, "rse": rse, "converged": rse <= rse_target}
+            "p99_us": float(q[5]), "trimmed_mean_us": float(mid.mean()), "n_samples": n, "rse": rse,
+            "converged": rse <= rse_target}
 
 
 def pool(results: list[TimingResult], rse_target: float = 0.01) -> TimingResult:

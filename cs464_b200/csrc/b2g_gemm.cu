@@ -102,6 +102,10 @@ struct KParams {
   void* out;
   int64_t out_si, out_sj, out_split_stride;
   int32_t out_kind, vec_ok;
+  // Row-major output written through a 4 KB shared staging tile per epilogue warp (non-swapped tiles, 16-byte rows,
+  // whole 16-byte pieces): the staging area starts `epi_stage_off` bytes after the operand ring.
+  int32_t stage_c;
+  uint32_t epi_stage_off;
   int* status;
   uint64_t timeout_ns;
   // stream-K: workers (CTAs, or CTA pairs) share sk_iters = tiles * num_kb K blocks in equal contiguous slices; a tile
@@ -319,6 +323,29 @@ __device__ __forceinline__ void store_chunk(const KParams& p, int split, int64_t
       if (j < ncol && col0 + j < p.rows_b) o[(col0 + j) * p.out_sj] = cvt_one(__uint_as_float(v[j]), bf);
     }
   }
+}
+
+// 32 rows x 128 bytes of output through shared memory: lane r writes row r's eight 16-byte pieces (four at a time,
+// from `j0`), with the piece index XOR-ed by (row & 7), which keeps both the row-wise writes and the piece-wise reads
+// free of bank conflicts; `stage_flush` then writes four whole 128-byte row segments per global store instruction
+// instead of 32 scattered 16-byte pieces (the load/store unit, not HBM, bounds the direct path). `rows` / `pieces`:
+// how many of the 32 rows and 8 pieces lie inside C.
+__device__ __forceinline__ void stage_write4(uint32_t stg, int lane, int j0, const uint4 (&pc)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) st_shared_v4(stg + lane * 128 + (((j0 + j) ^ (lane & 7)) << 4), pc[j]);
+}
+
+__device__ __forceinline__ void stage_flush(uint32_t stg, int lane, uint8_t* base, int64_t row_bytes, int rows,
+                                            int pieces) {
+  __syncwarp();
+  const int pp = lane & 7;
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    const int rr = 4 * s + (lane >> 3);
+    const uint4 x = ld_shared_v4(stg + rr * 128 + ((pp ^ (rr & 7)) << 4));
+    if (rr < rows && pp < pieces) *reinterpret_cast<uint4*>(base + rr * row_bytes + pp * 16) = x;
+  }
+  __syncwarp();
 }
 
 // One CTA (PAIR = 0) or one CTA of a pair (PAIR = 1, cluster of 2, cta_group::2 MMAs of M = 256).
@@ -629,6 +656,69 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
         if (row0 >= p.rows_a) break;
         const int64_t row = row0 + lane;
         const int row_local = h * 128 + q * 32 + lane;  // row within this CTA's part of the tile
+        if (p.stage_c && !contrib && !owner) {
+          const uint32_t stg = data + p.epi_stage_off + static_cast<uint32_t>(e) * 4096u;
+          const int rows_in = p.rows_a - row0 < 32 ? static_cast<int>(p.rows_a - row0) : 32;
+          if (p.out_kind == OUT_F32_PARTIAL) {  // 32 fp32 columns per 128-byte row
+            float* ob = static_cast<float*>(p.out) + static_cast<int64_t>(w.split) * p.out_split_stride;
+            for (int c = grp; c < nchunks; c += kGroups) {
+              const int64_t col0 = static_cast<int64_t>(w.tn) * p.tile_n + c * 32;
+              if (col0 >= p.rows_b) break;
+              uint32_t v[32];
+              if (zero) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = 0u;
+              } else {
+                tmem_ld_32cols(tmem_base + acc * p.acc_cols + h * p.tile_n + c * 32 + (static_cast<uint32_t>(q * 32) << 16),
+                               v);
+                tmem_ld_wait();
+              }
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                uint4 pc[4];
+#pragma unroll
+                for (int k4 = 0; k4 < 4; ++k4)
+                  pc[k4] = make_uint4(v[16 * hh + 4 * k4], v[16 * hh + 4 * k4 + 1], v[16 * hh + 4 * k4 + 2],
+                                      v[16 * hh + 4 * k4 + 3]);
+                stage_write4(stg, lane, 4 * hh, pc);
+              }
+              stage_flush(stg, lane, reinterpret_cast<uint8_t*>(ob + row0 * p.out_si + col0), p.out_si * 4, rows_in,
+                          (p.rows_b - col0) / 4 < 8 ? static_cast<int>((p.rows_b - col0) / 4) : 8);
+            }
+          } else {  // 64 half-precision columns (two TMEM chunks) per 128-byte row
+            const int bf = p.out_kind == OUT_BF16;
+            uint16_t* ob = static_cast<uint16_t*>(p.out);
+            for (int c2 = grp; 2 * c2 < nchunks; c2 += kGroups) {
+              const int64_t col0 = static_cast<int64_t>(w.tn) * p.tile_n + c2 * 64;
+              if (col0 >= p.rows_b) break;
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                uint32_t v[32];
+                if (zero) {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] = 0u;
+                } else {
+                  tmem_ld_32cols(tmem_base + acc * p.acc_cols + h * p.tile_n + c2 * 64 + hh * 32 +
+                                     (static_cast<uint32_t>(q * 32) << 16),
+                                 v);
+                  tmem_ld_wait();
+                }
+                uint4 pc[4];
+#pragma unroll
+                for (int k4 = 0; k4 < 4; ++k4) {
+                  pc[k4].x = cvt_pair(__uint_as_float(v[8 * k4 + 0]), __uint_as_float(v[8 * k4 + 1]), bf);
+                  pc[k4].y = cvt_pair(__uint_as_float(v[8 * k4 + 2]), __uint_as_float(v[8 * k4 + 3]), bf);
+                  pc[k4].z = cvt_pair(__uint_as_float(v[8 * k4 + 4]), __uint_as_float(v[8 * k4 + 5]), bf);
+                  pc[k4].w = cvt_pair(__uint_as_float(v[8 * k4 + 6]), __uint_as_float(v[8 * k4 + 7]), bf);
+                }
+                stage_write4(stg, lane, 4 * hh, pc);
+              }
+              stage_flush(stg, lane, reinterpret_cast<uint8_t*>(ob + row0 * p.out_si + col0), p.out_si * 2, rows_in,
+                          (p.rows_b - col0) / 8 < 8 ? static_cast<int>((p.rows_b - col0) / 8) : 8);
+            }
+          }
+          continue;
+        }
         for (int c = grp; c < nchunks; c += kGroups) {
           if (static_cast<int64_t>(w.tn) * p.tile_n + c * 32 >= p.rows_b) break;
           const int ncol = min(32, p.tile_n - c * 32);
@@ -1248,6 +1338,18 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
     p->pair = g.pair;
     p->threads = (2 + g.epi_warps) * 32;
     p->smem = g.smem;
+    {
+      // staged epilogue: row-major C (or the fp32 partials) in whole 16-byte pieces, 64-column half-precision chunk
+      // pairs, and room for 4 KB per epilogue warp next to the ring
+      const size_t staging = static_cast<size_t>(g.epi_warps) * 4096;
+      const bool partial = cfg->split_k > 1;
+      const bool pieces_ok = partial ? (N % 4 == 0) : (N % 8 == 0 && g.tile_n % 64 == 0);
+      if (!g.swapped && !g.streamk && k.vec_ok && pieces_ok && g.smem + staging <= kMaxSmemPerCta) {
+        k.stage_c = 1;
+        k.epi_stage_off = static_cast<uint32_t>(static_cast<size_t>(g.cta_m + g.cta_n) * g.bk * 2 * g.stages);
+        p->smem = g.smem + staging;
+      }
+    }
     // grid in work units (CTAs, or CTA pairs)
     int64_t grid = g.units;
     if (cfg->schedule == B2G_SCHED_PERSISTENT || cfg->schedule == B2G_SCHED_STREAMK) {

@@ -42,7 +42,7 @@ FALLBACK_PEAK_TFLOPS = 1590.0
 FLUSH_BYTES = 1 << 30
 # DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of that exact launch
 # (profiles/gemm_16384_256x256x64_full.md): {(size, config key): bytes}. Other selections report null.
-TRAFFIC_BYTES = {(16384, "bm256_bn256_bk64_w4_s3_g8_sk1"): 6.764298e9 + 0.527529e9}
+TRAFFIC_BYTES = {(16384, "bm256_bn256_bk64_w4_s3_g8_sk1"): 6.761165e9 + 0.528053e9}
 
 
 def parse_args():

@@ -5,7 +5,9 @@ Workload: M = N = K in {256, 512, 1024, 2048, 4096, 8192, 16384}, row-major A[M,
 entries cast to fp16 (CUDA generator, seed 0), fp32 accumulate, fp16 output. One step = one GEMM of every size, each
 preceded by an L2 flush (a 1 GiB write, outside the GEMM's timed interval). `value` = sum of 2*n^3 over the sizes, all
 steps and all ranks, divided by the summed device time of the GEMMs (CUDA events on the launching stream, max over
-ranks). Each size runs the config the shipped zero-search rule (cs464_b200.select) or the winner cache picks.
+ranks). Each size runs the config the library's first-use selection picks before the timed steps: the shipped
+ranker's top 3 plus the zero-search rule's config (cs464_b200.select), each validated and short-timed on the size's
+inputs (cs464_b200.search.measure / choose), the fastest kept; `--config KEY` forces one config instead.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
@@ -182,6 +184,9 @@ def main():
 
     from cs464_b200.keys import parse_key
     from cs464_b200.matmul import B200Matmul, matmul
+    from cs464_b200.gate import reference
+    from cs464_b200.ranker import default_ranker
+    from cs464_b200.search import FAMILY, choose, measure
     from cs464_b200.select import heuristic_config
 
     torch.cuda.set_device(local)
@@ -200,13 +205,24 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    ranker = default_ranker() if not args.config else None
+
+    def select_config(a, b):
+        """First-use selection for one square size: ranker top 3 + the zero-search rule, short-timed."""
+        n = a.shape[0]
+        keys = list(dict.fromkeys(ranker.rank(n, n, n, 3, order="diverse") + [heuristic_config(n, n, n).key()]))
+        r = measure(n, n, n, torch.float16, [(FAMILY, k, B200Matmul(parse_key(k))) for k in keys],
+                    inputs=(a, b, reference(a, b)))
+        choice = choose(r["candidates"])
+        return parse_key(choice["key"]) if choice.get("key") else heuristic_config(n, n, n)
+
     sizes = args.sizes_list or SIZES
     g = torch.Generator(device=dev).manual_seed(0)
     work = []
     for n in sizes:
         a = torch.randn((n, n), generator=g, device=dev, dtype=torch.float32).to(torch.float16)
         b = torch.randn((n, n), generator=g, device=dev, dtype=torch.float32).to(torch.float16)
-        cfg = parse_key(args.config) if args.config else heuristic_config(n, n, n)
+        cfg = parse_key(args.config) if args.config else select_config(a, b)
         c = torch.empty((n, n), device=dev, dtype=torch.float16)
         run = B200Matmul(cfg).make_runner(a, b, out=c)
         work.append({"n": n, "a": a, "b": b, "c": c, "cfg": cfg, "run": run, "flops": 2.0 * n ** 3})

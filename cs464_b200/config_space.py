@@ -43,9 +43,9 @@ class HwLimits:
     tmem_columns: int = TMEM_COLUMNS
 
     @classmethod
-    def from_device(cls, device: int = 0) -> "HwLimits":
+    def from_device(cls, device: int | None = None) -> "HwLimits":
         import torch
-        p = torch.cuda.get_device_properties(device)
+        p = torch.cuda.get_device_properties(torch.cuda.current_device() if device is None else device)
         return cls(p.shared_memory_per_block_optin, p.regs_per_multiprocessor, p.multi_processor_count)
 
     @classmethod

@@ -146,9 +146,12 @@ def _backlog(seconds: float, device: int) -> None:
         torch.cuda._sleep(int(min(seconds, 0.2) * _sleep_cycles_per_s(device)))
 
 
-def gpu_telemetry(device: int = 0) -> dict:
-    """SM clock, temperature and power via NVML when available (best effort, never raises)."""
+def gpu_telemetry(device: int | None = None) -> dict:
+    """SM clock, temperature and power via NVML when available (best effort, never raises). `device`: the torch
+    device index (default: the current device)."""
     try:
+        if device is None:
+            device = torch.cuda.current_device()
         import pynvml
         pynvml.nvmlInit()
         idx = device
@@ -172,9 +175,12 @@ def gpu_telemetry(device: int = 0) -> dict:
         return {}
 
 
-def benchmark(fn: Callable[[], object], cfg: TimingConfig | None = None, device: int = 0) -> TimingResult:
-    """Time `fn`, which must only enqueue GPU work on the current stream."""
+def benchmark(fn: Callable[[], object], cfg: TimingConfig | None = None, device: int | None = None) -> TimingResult:
+    """Time `fn`, which must only enqueue GPU work on the current stream. `device`: the torch device index to time on
+    (default: the current device, so a process driving GPU r keeps working on GPU r)."""
     cfg = cfg or TimingConfig()
+    if device is None:
+        device = torch.cuda.current_device()
     torch.cuda.set_device(device)
     flush = _flusher(cfg.flush_bytes, device) if cfg.cache_mode == "cold" else None
 

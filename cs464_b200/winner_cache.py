@@ -39,9 +39,9 @@ def kernel_src_hash() -> str:
     return _abi.source_hash()
 
 
-def hw_id(device: int = 0) -> str:
+def hw_id(device: int | None = None) -> str:
     import torch
-    p = torch.cuda.get_device_properties(device)
+    p = torch.cuda.get_device_properties(torch.cuda.current_device() if device is None else device)
     return f"{p.name}|sm{p.major}{p.minor}|{p.multi_processor_count}sm|{round(p.total_memory / 2**30)}GiB"
 
 
@@ -53,7 +53,7 @@ def clock_lock_declared(value: str | None = None) -> str | None:
     return "unlocked" if v in ("none", "off", "0", "unlocked") else v
 
 
-def environment(device: int = 0, clock_lock: str | None = None, extra: dict | None = None) -> dict:
+def environment(device: int | None = None, clock_lock: str | None = None, extra: dict | None = None) -> dict:
     import torch
     env = {"hw_id": hw_id(device), "kernel_src": kernel_src_hash(), "torch": torch.__version__,
            "cuda_runtime": torch.version.cuda, "driver": _driver_version(), "clock_lock": clock_lock_declared(clock_lock)}

@@ -146,3 +146,24 @@ def test_cublaslt_comparator_candidates_valid():
         a, b = gate.make_inputs(M, N, K)
         for c in cs:
             assert gate.validate(c, M, N, K, inputs=(a, b), norm_rel=True).valid, (M, N, K, c.key)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs a second GPU")
+def test_timing_and_selection_stay_on_the_current_device():
+    """A process that drives GPU 1 (a torchrun rank, a shard worker) times and selects on GPU 1: the timer does not
+    switch the process back to GPU 0 behind the caller's back."""
+    from cs464_b200.keys import parse_key
+    from cs464_b200.search import FAMILY, choose, measure
+    make_inputs, reference = gate.make_inputs, gate.reference
+    prev = torch.cuda.current_device()
+    try:
+        torch.cuda.set_device(1)
+        a, b = make_inputs(256, 256, 256, torch.float16)
+        assert a.device.index == 1
+        keys = ["bm128_bn128_bk64_w4_s4_g8_sk1", "bm128_bn64_bk64_w4_s4_g8_sk1"]
+        r = measure(256, 256, 256, torch.float16, [(FAMILY, k, B200Matmul(parse_key(k))) for k in keys],
+                    inputs=(a, b, reference(a, b)))
+        assert choose(r["candidates"])["key"] in keys
+        assert torch.cuda.current_device() == 1
+    finally:
+        torch.cuda.set_device(prev)

@@ -1513,6 +1513,14 @@ int32_t b2g_plan_create(const b2g_config* cfg, const b2g_problem* prob, const vo
 int32_t b2g_plan_launch(const b2g_plan* p, void* stream) {
   if (!p) return fail(B2G_ERR_INVALID_ARG, "null plan");
   if (p->empty) return B2G_OK;
+  // A plan's tensor maps and buffers live on the device it was made on; launching it while another device is
+  // current would run the kernel against memory that device cannot reach.
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != p->device) {
+    char buf[128];
+    snprintf(buf, sizeof buf, "plan was made on device %d but device %d is current", p->device, cur);
+    return fail(B2G_ERR_INVALID_ARG, buf);
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p->pack_a) {
     pack_kernel<<<grid_for(p->pa_outer * p->pa_inner, 256), 256, 0, st>>>(

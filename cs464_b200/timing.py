@@ -187,13 +187,15 @@ def benchmark(fn: Callable[[], object], cfg: TimingConfig | None = None, device:
     fn()  # first call: plan set-up, never timed
     torch.cuda.synchronize()
     if cfg.use_graph:
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
+        # Capture on a stream of this device: torch's default capture stream belongs to whichever GPU was current at
+        # the process's first capture, and capturing on it would switch a process that drives GPU 1 to GPU 0.
+        side = torch.cuda.Stream(device=device)
+        side.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(side):
             fn()
-        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.current_stream(device).wait_stream(side)
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        with torch.cuda.graph(graph, stream=side):
             for _ in range(cfg.batch):
                 fn()
         run = graph.replay

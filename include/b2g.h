@@ -116,8 +116,9 @@ int32_t b2g_smem_bytes(const b2g_config* cfg, const b2g_problem* prob, size_t* b
    output). Pointers are captured in the plan: a plan runs on exactly these buffers. */
 int32_t b2g_plan_create(const b2g_config* cfg, const b2g_problem* prob, const void* A, const void* B, void* C,
                         void* workspace, size_t workspace_bytes, int32_t* status, b2g_plan** out);
-/* Enqueue the plan's kernels on `stream` (cudaStream_t). No allocation, no host synchronisation: capturable into a
-   CUDA graph. Returns B2G_OK or B2G_ERR_CUDA (launch error). */
+/* Enqueue the plan's kernels on `stream` (cudaStream_t, a stream of the plan's device). No allocation, no host
+   synchronisation: capturable into a CUDA graph. Returns B2G_OK, B2G_ERR_INVALID_ARG when the current device is not
+   the one the plan was made on (nothing is launched), or B2G_ERR_CUDA (launch error). */
 int32_t b2g_plan_launch(const b2g_plan* plan, void* stream);
 /* number of kernels b2g_plan_launch enqueues (packing, GEMM, split-K reduce) */
 int32_t b2g_plan_num_kernels(const b2g_plan* plan);

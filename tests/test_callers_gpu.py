@@ -167,3 +167,21 @@ def test_timing_and_selection_stay_on_the_current_device():
         assert torch.cuda.current_device() == 1
     finally:
         torch.cuda.set_device(prev)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs a second GPU")
+def test_plan_refuses_to_launch_on_another_device():
+    """A runner made for GPU 1 raises instead of launching while GPU 0 is current."""
+    from cs464_b200 import _abi
+    prev = torch.cuda.current_device()
+    try:
+        torch.cuda.set_device(1)
+        a, b = gate.make_inputs(128, 128, 128, torch.float16)
+        run = B200Matmul(MatmulConfig(128, 128, 64)).make_runner(a, b)
+        run()
+        torch.cuda.synchronize()
+        torch.cuda.set_device(0)
+        with pytest.raises(_abi.B2GError, match="plan was made on device 1"):
+            run()
+    finally:
+        torch.cuda.set_device(prev)

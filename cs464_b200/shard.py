@@ -158,8 +158,16 @@ def summarize(out_dir: str, rank_stats: list[dict]) -> dict:
             "gap_mean": statistics.fmean(gaps) if gaps else None}
 
 
+def worker_threads(gpus: int) -> int:
+    """Host threads per search process: the host's cores split between the processes. The ranker's tree-ensemble
+    predict and torch's CPU ops start one OpenMP thread per core in every process; with one process per GPU those
+    spinning pools oversubscribe the host and the selector's step slows several-fold."""
+    return max(1, (os.cpu_count() or 1) // max(1, gpus))
+
+
 def _worker(rank: int, device: int, args: dict, results):
     os.environ["CUDA_VISIBLE_DEVICES"] = str(device)
+    os.environ.setdefault("OMP_NUM_THREADS", str(worker_threads(args.get("gpus", 1))))
     res = run_rank(rank, args["queue"], args["out"], args["cache"], k=args["k"], space=args["space"],
                    max_shapes=args.get("max_shapes"))
     results.put(res)
@@ -201,7 +209,7 @@ def main(argv=None) -> dict:
         ShapeQueue.create(queue, shapes)
         ctx = mp.get_context("spawn")
         results = ctx.Queue()
-        args = {"queue": queue, "out": str(out), "cache": cache, "k": a.k, "space": a.space}
+        args = {"queue": queue, "out": str(out), "cache": cache, "k": a.k, "space": a.space, "gpus": a.gpus}
         procs = [ctx.Process(target=_worker, args=(r, r, args, results)) for r in range(a.gpus)]
         for p in procs:
             p.start()

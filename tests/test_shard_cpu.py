@@ -57,3 +57,11 @@ def test_two_ranks_claim_every_shape_once(tmp_path):
 def test_queue_orders_biggest_first(tmp_path):
     q = shard.ShapeQueue.create(tmp_path / "q.jsonl", [{"M": 1, "N": 1, "K": 1}, {"M": 64, "N": 64, "K": 64}])
     assert q.claim(0)[0] == 1 and q.claim(0)[0] == 0 and q.claim(0) is None
+
+
+def test_worker_threads_split_the_host():
+    from cs464_b200.shard import worker_threads
+    n = os.cpu_count() or 1
+    assert worker_threads(1) == n
+    assert worker_threads(8) == max(1, n // 8)
+    assert worker_threads(10 ** 6) == 1

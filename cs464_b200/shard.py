@@ -95,7 +95,9 @@ def search_one(shape: dict, *, k: int = 3, space: int | None = None, ranker=None
     if ranker is None:
         from cs464_b200.search import _ranker_default
         ranker = _ranker_default()
+    t_rank = time.perf_counter()
     keys = ranker.rank(M, N, K, k, order="diverse")
+    t_rank = time.perf_counter() - t_rank
     sel = measure(M, N, K, torch.float16, [("b200_sm100a_v1", key, B200Matmul(parse_key(key))) for key in keys],
                   inputs=(a, b, ref))
     choice = choose(sel["candidates"])
@@ -114,7 +116,9 @@ def search_one(shape: dict, *, k: int = 3, space: int | None = None, ranker=None
             "screen": [[r["key"], round(r["us"], 3)] for r in scr["rows"] if r["status"] in ("ok", "slow")],
             "chosen_screen_us": us.get(chosen), "best_key": scr["best_key"], "best_us": scr["best_us"], "gap": gap,
             "n_screened": scr["n_configs"], "n_ok": sum(1 for r in scr["rows"] if r["status"] == "ok"),
-            "select_s": t_select, "wall_s": time.perf_counter() - t0}
+            "select_s": t_select, "rank_s": t_rank,
+            "validate_s": sum(x.get("setup_s", 0.0) for x in sel["candidates"]),
+            "timing_s": sum(x.get("time_s", 0.0) for x in sel["candidates"]), "wall_s": time.perf_counter() - t0}
 
 
 def run_rank(rank: int, queue_path: str, out_dir: str, cache_path: str | None, *, k: int = 3, space: int | None = None,
@@ -160,14 +164,26 @@ def summarize(out_dir: str, rank_stats: list[dict]) -> dict:
 
 def worker_threads(gpus: int) -> int:
     """Host threads per search process: the host's cores split between the processes. The ranker's tree-ensemble
-    predict and torch's CPU ops start one OpenMP thread per core in every process; with one process per GPU those
-    spinning pools oversubscribe the host and the selector's step slows several-fold."""
+    predict starts one OpenMP thread per core in every process; with one process per GPU those spinning pools
+    oversubscribe the host (measured on 2 GPUs: the ranking step went from 33 ms to 2.2 s per shape)."""
     return max(1, (os.cpu_count() or 1) // max(1, gpus))
+
+
+def limit_host_threads(n: int) -> None:
+    """Cap this process's CPU thread pools (OpenMP of the ranker's predict, BLAS, torch's intra-op pool) at n."""
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(n)
+    except ImportError:
+        pass
+    import torch
+    torch.set_num_threads(n)
 
 
 def _worker(rank: int, device: int, args: dict, results):
     os.environ["CUDA_VISIBLE_DEVICES"] = str(device)
-    os.environ.setdefault("OMP_NUM_THREADS", str(worker_threads(args.get("gpus", 1))))
+    limit_host_threads(worker_threads(args.get("gpus", 1)))
     res = run_rank(rank, args["queue"], args["out"], args["cache"], k=args["k"], space=args["space"],
                    max_shapes=args.get("max_shapes"))
     results.put(res)
@@ -194,6 +210,7 @@ def main(argv=None) -> dict:
         import torch
         import torch.distributed as dist
         rank = int(os.environ["RANK"])
+        limit_host_threads(worker_threads(int(os.environ.get("LOCAL_WORLD_SIZE", world))))
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
         dist.init_process_group("gloo")
         if rank == 0:

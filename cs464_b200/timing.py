@@ -194,10 +194,16 @@ def benchmark(fn: Callable[[], object], cfg: TimingConfig | None = None, device:
         with torch.cuda.stream(side):
             fn()
         torch.cuda.current_stream(device).wait_stream(side)
+        # Captured directly: `torch.cuda.graph` also runs a full Python garbage collection and empties the allocator
+        # cache before every capture, host work that dominated the selector's step for small shapes.
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=side):
-            for _ in range(cfg.batch):
-                fn()
+        with torch.cuda.stream(side):
+            graph.capture_begin()
+            try:
+                for _ in range(cfg.batch):
+                    fn()
+            finally:
+                graph.capture_end()
         run = graph.replay
     elif cfg.batch > 1:
         def run():

@@ -354,6 +354,9 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     gemm_kernel(const __grid_constant__ KParams p, const __grid_constant__ CUtensorMap tma_a,
                 const __grid_constant__ CUtensorMap tma_b) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // Let a programmatically dependent launch (the split-K reduce) be scheduled once every CTA of this grid is
+  // running; the dependent waits for this grid's completion before it reads anything.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const uint32_t ctl = smem_addr(smem_raw);
   const uint32_t data = (ctl + kCtlBytes + 1023u) & ~1023u;
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem_raw + OFF_ABORT);
@@ -821,6 +824,9 @@ __global__ void pack_kernel(const uint16_t* __restrict__ src, int64_t s_outer, i
 // kernels/triton_matmul.py:85-92). vec: N % 4 == 0, scn == 1, scm % 4 == 0 and C 8-byte aligned.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ C, int64_t M, int64_t N,
                                      int64_t scm, int64_t scn, int split, int bf16, int vec) {
+  // Launched as a programmatic dependent of the GEMM (its launch overlaps the GEMM's tail): wait until the GEMM
+  // grid has completed and its partials are visible. Without that launch attribute this returns at once.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t MN = M * N;
   const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
   uint16_t* c = static_cast<uint16_t*>(C);
@@ -1557,8 +1563,19 @@ int32_t b2g_plan_launch(const b2g_plan* p, void* stream) {
   }
   if (p->reduce) {
     const int64_t work = p->r_vec ? p->r_M * p->r_N / 4 : p->r_M * p->r_N;
-    splitk_reduce_kernel<<<grid_for(work, 256), 256, 0, st>>>(p->r_ws, p->r_c, p->r_M, p->r_N, p->r_scm, p->r_scn,
-                                                                p->r_split, p->r_bf16, p->r_vec);
+    cudaLaunchConfig_t lc = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.gridDim = dim3(grid_for(work, 256), 1, 1);
+    lc.blockDim = dim3(256, 1, 1);
+    lc.dynamicSmemBytes = 0;
+    lc.stream = st;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    cudaError_t le = cudaLaunchKernelEx(&lc, splitk_reduce_kernel, p->r_ws, p->r_c, p->r_M, p->r_N, p->r_scm,
+                                        p->r_scn, p->r_split, p->r_bf16, p->r_vec);
+    if (le != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("reduce launch: ") + cudaGetErrorString(le));
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));

@@ -103,18 +103,8 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16 (fp16 or bf16 inputs, fp32 accumulator), issued by one thread.
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// The same MMA executed by a converged warp with only lane 0 issuing it (predicated, not a branch): the warp's
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16 (fp16 or bf16 inputs, fp32 accumulator; `accumulate` = 0
+// overwrites D). Executed by a converged warp with only lane 0 issuing it (predicated, not a branch): the warp's
 // operands stay uniform, so the issue does not pay a per-instruction move from per-thread registers.
 __device__ __forceinline__ void umma_f16_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                            uint32_t accumulate) {
@@ -128,7 +118,8 @@ __device__ __forceinline__ void umma_f16_w(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
-// Lane 0 of a converged warp commits (the lane that issued the warp's MMAs).
+// Arrive once on `bar` when every tcgen05 operation issued before by this lane has completed; lane 0 of a converged
+// warp commits (the lane that issued the warp's MMAs).
 __device__ __forceinline__ void umma_commit_w(uint32_t bar) {
   asm volatile(
       "{\n\t.reg .pred q;\n\t.reg .u32 l;\n\t"
@@ -136,11 +127,6 @@ __device__ __forceinline__ void umma_commit_w(uint32_t bar) {
       "setp.eq.u32 q, l, 0;\n\t"
       "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
       : "memory");
-}
-
-// Arrive once on `bar` when every tcgen05 operation this thread issued before has completed.
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -239,19 +225,8 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
-// M = 256 MMA over the CTA pair: A rows 0-127 and B columns 0..N/2-1 from the leader's shared memory, the rest from
-// the peer's at the same offsets; D rows 0-127 in the leader's tensor memory, 128-255 in the peer's.
-__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                              uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// umma_f16_pair / umma_commit_pair issued by lane 0 of a converged warp (see umma_f16_w)
+// cta_group::2 forms (the pair's leader issues for both CTAs, M = 256), issued by lane 0 of a converged warp; the
+// commit arrives on the barrier at shared::cluster address `bar_cluster` once the pair's prior MMAs completed
 __device__ __forceinline__ void umma_f16_pair_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                                 uint32_t accumulate) {
   asm volatile(
@@ -271,12 +246,6 @@ __device__ __forceinline__ void umma_commit_pair_w(uint32_t bar_cluster) {
       "setp.eq.u32 q, l, 0;\n\t"
       "@q tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar_cluster)
       : "memory");
-}
-
-// arrive once on the barrier at shared::cluster address `bar_cluster` when the pair's prior MMAs have completed
-__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
-               : "memory");
 }
 
 // ---------------------------------------------------------------- descriptors

@@ -1,4 +1,4 @@
-"""Per-shape comparison of the sm_100a family with cuBLASLt and torch.matmul (BASELINE configs 3 and 4).
+"""Per-shape comparison of the sm_100a family with cuBLASLt and torch.matmul (BASELINE.json configs 3 and 4).
 
 For every shape of a suite, on one GPU, with one timing protocol (cold L2, CUDA events, trimmed mean of the samples):
   * `sel`   the family's zero-search pick: the ranker's top-k validated and short-timed, the fastest kept

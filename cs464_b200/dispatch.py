@@ -8,7 +8,7 @@ torch takes at least `min_kernel_us` and the winner saves at least max(min_savin
 the entry was timed under a declared clock lock) (lscli/client.py:52-57, :99-113). Everything else goes to torch.
 Under autograd the forward runs the selected kernel and the backward the original torch matmul.
 
-MAX_DIM is 65536: the kernels take any dimension below 2^31, and BASELINE config 4 needs N = 28672, above the
+MAX_DIM is 65536: the kernels take any dimension below 2^31, and BASELINE.json config 4 needs N = 28672, above the
 reference's 16384.
 """
 from __future__ import annotations

@@ -7,7 +7,7 @@ Pass criterion, elementwise, as in the reference (tune/correctness.py:116-127):
     |C - ref| <= rtol * |ref| + atol_frac * sqrt(K)
 The output is pre-filled with NaN, so a kernel that leaves elements unwritten fails (`non_finite_output(n)`).
 
-The north star adds a scale-free bound that does not assume unit-variance inputs (BASELINE config 4 draws weights from
+The north star adds a scale-free bound that does not assume unit-variance inputs (BASELINE.json config 4 draws weights from
 N(0, 0.02^2), where atol_frac * sqrt(K) is 50x too loose):
     |C - ref|_ij <= 2e-3 * ||A_i,:||_2 * ||B_:,j||_2          (`check_norm_relative`, `validate(..., norm_rel=True)`)
 
@@ -46,7 +46,7 @@ def strict_fp32():
 def make_inputs(M: int, N: int, K: int, dtype=torch.float16, seed: int = 0, device: str = "cuda",
                 scale_b: float = 1.0):
     """Seeded A [M,K] and B [K,N]: one generator on `device`, randn A then B in fp32, cast (tune/correctness.py:36-40).
-    `scale_b` multiplies B before the cast (BASELINE config 4's weights are N(0, 0.02^2))."""
+    `scale_b` multiplies B before the cast (BASELINE.json config 4's weights are N(0, 0.02^2))."""
     g = torch.Generator(device=device).manual_seed(seed)
     a = torch.randn((M, K), generator=g, device=device, dtype=torch.float32).to(dtype)
     b = torch.randn((K, N), generator=g, device=device, dtype=torch.float32)

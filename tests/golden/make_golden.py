@@ -10,7 +10,7 @@ It imports, from the reference:
 and writes:
   * gemm_cases.npz + gemm_cases.json  inputs (CPU generator), the reference's fp32 result, and the gate's verdicts on
                                       the rounded result and on planted mistakes (a corrupted tile, a NaN row);
-  * inputs_hash.json                  sha256 of make_inputs bytes for the BASELINE config-1 shape (1024^3, seed 0)
+  * inputs_hash.json                  sha256 of make_inputs bytes for the BASELINE.json config-1 shape (1024^3, seed 0)
                                       and other seeds/shapes, so the CPU generator stream is pinned without 4 MB arrays;
   * config_rules.json                 the reference's shape-rule verdicts and key strings on a sample of its space,
                                       plus its static-prune counts for the RTX 3080 limits it was written for.

@@ -86,6 +86,34 @@ def test_split_k_uneven_k(split_k, bm):
     _assert_parity(c, oracle.gemm_f32(a, b), a, b, 1000)
 
 
+@pytest.mark.parametrize("split_k", [1, 3])
+@pytest.mark.parametrize("cfg", [MatmulConfig(128, 128, 64, num_stages=4, GROUP_M=1),
+                                 MatmulConfig(256, 256, 64, num_stages=3, GROUP_M=1),
+                                 MatmulConfig(256, 128, 64, num_stages=4, GROUP_M=1, CLUSTER=2)],
+                         ids=lambda c: c.key())
+@pytest.mark.parametrize("shape", [(100, 72, 640), (300, 520, 700), (33, 136, 256)])
+def test_staged_epilogue_edges(cfg, split_k, shape):
+    """The epilogue that writes rows through shared memory, at C's edges: rows past M inside a 32-row slab, and a
+    last 64-column group (32 for the fp32 split-K partials) holding only some 16-byte pieces. Every element must be
+    written exactly as the oracle has it, none outside C (the output starts NaN and C is a view inside a larger
+    NaN-filled buffer)."""
+    M, N, K = shape
+    cfg = MatmulConfig(cfg.BLOCK_M, cfg.BLOCK_N, cfg.BLOCK_K, num_warps=cfg.num_warps, num_stages=cfg.num_stages,
+                       GROUP_M=cfg.GROUP_M, SPLIT_K=split_k, CLUSTER=cfg.CLUSTER)
+    a_cpu, b_cpu = oracle.make_inputs(M, N, K, seed=7)
+    big = torch.full((M + 3, N + 16), float("nan"), device="cuda", dtype=torch.float16)
+    out = big[1:M + 1, 8:N + 8]  # 16-byte-aligned start, row stride N + 16 (a multiple of 8)
+    run = B200Matmul(cfg).make_runner(a_cpu.cuda(), b_cpu.cuda(), out=out)
+    c = run()
+    torch.cuda.synchronize()
+    run.raise_on_status()
+    _assert_parity(c, oracle.gemm_f32(a_cpu, b_cpu), a_cpu, b_cpu, K)
+    rest = big.clone()
+    rest[1:M + 1, 8:N + 8] = 0
+    assert torch.isnan(rest[0]).all() and torch.isnan(rest[M + 1:]).all()
+    assert torch.isnan(rest[:, :8]).all() and torch.isnan(rest[:, N + 8:]).all()
+
+
 @pytest.mark.parametrize("cfg", [MatmulConfig(256, 256, 64, num_stages=3, PERSISTENT=2),
                                  MatmulConfig(256, 256, 64, num_stages=6, CLUSTER=2, PERSISTENT=2),
                                  MatmulConfig(16, 256, 64, num_stages=6, GROUP_M=1, PERSISTENT=2)],

@@ -256,3 +256,29 @@ def test_square_16384_properties():
         if cfg.SPLIT_K > 1:
             assert torch.equal(c, run())
         del c, err
+
+
+def test_split_k_plan_replays_from_a_cuda_graph():
+    """The split-K reduce is a programmatic dependent launch of the GEMM; a runner captured into a CUDA graph (as the
+    timer does) replays both kernels in order and gives the same bits as a direct call."""
+    cfg = MatmulConfig(128, 128, 64, num_stages=4, GROUP_M=1, SPLIT_K=4)
+    a_cpu, b_cpu = oracle.make_inputs(192, 256, 2048, seed=9)
+    a, b = a_cpu.cuda(), b_cpu.cuda()
+    run = B200Matmul(cfg).make_runner(a, b)
+    direct = run().clone()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        run()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        g.capture_begin()
+        run()
+        g.capture_end()
+    run.c.fill_(float("nan"))
+    g.replay()
+    torch.cuda.synchronize()
+    run.raise_on_status()
+    assert torch.equal(run.c, direct)
+    _assert_parity(run.c, oracle.gemm_f32(a_cpu, b_cpu), a_cpu, b_cpu, 2048)

@@ -264,3 +264,22 @@ def test_ranker_training_rows_and_default(tmp_path):
     rows = rk.rows_from_search([p])
     assert len(rows) == 2 and {r["key"] for r in rows} == {"bm128_bn128_bk64_w4_s6_g8_sk1", "bm16_bn128_bk128_w4_s6_g1_sk1"}
     assert hasattr(rk.default_ranker(), "rank")
+
+
+def test_placed_inputs_keep_values_and_alignment():
+    """Placements (tune/correctness.py:46-77) hold the same values at other addresses, shifted by whole MiB so the
+    allocator's alignment is kept; placement 0 is the plain inputs."""
+    from cs464_b200.gate import make_inputs, placed_inputs
+    a0, b0 = make_inputs(64, 48, 80, torch.float16, seed=3, device="cpu")
+    a, b, extra = placed_inputs(64, 48, 80, torch.float16, seed=3, placement=0, device="cpu")
+    assert extra is None and torch.equal(a, a0) and torch.equal(b, b0)
+    seen = set()
+    for placement in (1, 2, 3):
+        a, b, _ = placed_inputs(64, 48, 80, torch.float16, seed=3, placement=placement, device="cpu",
+                                avoid=frozenset(seen))
+        assert torch.equal(a, a0) and torch.equal(b, b0)
+        assert a.is_contiguous() and b.is_contiguous()
+        assert a.data_ptr() % 64 == 0 and b.data_ptr() % 64 == 0
+        seen |= {a.data_ptr(), b.data_ptr()}
+    again = placed_inputs(64, 48, 80, torch.float16, seed=3, placement=2, device="cpu")
+    assert torch.equal(again[0], a0)  # deterministic values for a given (seed, placement)

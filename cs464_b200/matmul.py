@@ -36,9 +36,9 @@ class MatmulConfig:
     num_stages shared-memory ring depth, GROUP_M L2 tile grouping, SPLIT_K deterministic K splits. BLOCK_M <= 64 runs
     the operand-swapped skinny form. PERSISTENT=1: one CTA per SM slot walks the tiles; 0: one CTA per (tile, split),
     the reference's grid (kernels/triton_matmul.py:99-100); 2: stream-K, persistent workers split tiles x K blocks
-    evenly and finish split tiles in K order (deterministic, needs SPLIT_K=1). CLUSTER=2: a pair of CTAs on two SMs computes each tile
-    with M=256 tcgen05 MMAs (BLOCK_M = 256, or BLOCK_N = 256 in the skinny form), each CTA loading half of A and half
-    of B."""
+    evenly and finish split tiles in K order (deterministic, needs SPLIT_K=1). CLUSTER=2: a pair of CTAs on two SMs
+    computes each tile with M=256 tcgen05 MMAs (BLOCK_M = 256, or BLOCK_N = 256 in the skinny form), each CTA loading
+    half of A and half of B."""
     BLOCK_M: int
     BLOCK_N: int
     BLOCK_K: int

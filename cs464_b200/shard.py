@@ -1,4 +1,4 @@
-"""Shape-sharded selector search over the GPUs of one host (the selector search sharded by shape).
+"""Shape-sharded selector search over the GPUs of one host.
 
 A GEMM runs on one GPU; what shards is the search: shapes are independent units. One process per GPU claims shapes
 from a shared work queue (a flock-protected JSONL of claims, biggest problems first, so long shapes do not end up

@@ -27,14 +27,13 @@ from cs464_b200.gate import make_inputs, reference, validate
 from cs464_b200.keys import parse_key
 from cs464_b200.matmul import B200Matmul
 from cs464_b200.search import choose, measure, screen_shape, shape_space
-from cs464_b200.timing import TimingConfig, benchmark
+from cs464_b200.timing import Protocol, measure_us
 
-FULL = TimingConfig(cache_mode="cold", warmup_ms=5.0, min_warmup_iters=2, min_reps=20, max_reps=100, target_rse=0.01,
-                    max_time_s=1.0, keep_raw=False)
+FULL = Protocol(mode="cold", samples=20, max_samples=100, warmup=3, ci_target=0.01, max_s=1.0)
 
 
 def _time(backend, a, b) -> float:
-    return benchmark(backend.make_runner(a, b), FULL).trimmed_mean_us
+    return measure_us(backend.make_runner(a, b), FULL, keep_samples=False).trimmed_us
 
 
 def compare_shape(shape: dict, *, k: int = 3, space: int = 0, lt_n: int = 16, ranker=None) -> dict:

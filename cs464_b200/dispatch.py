@@ -167,14 +167,14 @@ def torch_time_us(M: int, N: int, K: int, dtype=torch.float16) -> float:
     """torch.matmul's short cold time for the shape (the dispatch rule's comparator), measured like the candidates."""
     from cs464_b200.baselines import TorchMatmul
     from cs464_b200.gate import make_inputs
-    from cs464_b200.timing import benchmark, short_configs
+    from cs464_b200.timing import SHORT_COLD, measure_us
     a, b = make_inputs(M, N, K, dtype)
     mm = _ORIG.get("matmul", torch.matmul)
     run = TorchMatmul().make_runner(a, b)
     if mm is not torch.matmul:
         c = torch.empty((M, N), device=a.device, dtype=dtype)
         run = lambda: mm(a, b, out=c)  # noqa: E731  (the unpatched function while dispatch is on)
-    return benchmark(run, short_configs()[0]).median_us
+    return measure_us(run, SHORT_COLD, keep_samples=False).median_us
 
 
 def enable(cache=None, **settings) -> None:

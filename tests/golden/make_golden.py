@@ -1,6 +1,7 @@
 """Generate the golden fixtures under tests/golden/ by running the REFERENCE's own Python code.
 
-Run in the build container only (it needs the reference checkout; pass its path as argv[1], default /root/reference):
+Run where a checkout of the reference exists (pass its path as argv[1], or set $CS464_REFERENCE; by default a
+`reference` directory next to this repository's root):
     python tests/golden/make_golden.py /path/to/reference
 
 It imports, from the reference:
@@ -20,13 +21,15 @@ from __future__ import annotations
 
 import hashlib
 import json
+import os
 import sys
 from pathlib import Path
 
 import numpy as np
 
 OUT = Path(__file__).resolve().parent
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+REF = Path(sys.argv[1] if len(sys.argv) > 1 else
+           (os.environ.get("CS464_REFERENCE") or Path(__file__).resolve().parents[3] / "reference"))
 sys.path.insert(0, str(REF))
 
 import torch  # noqa: E402

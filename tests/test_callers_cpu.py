@@ -68,21 +68,38 @@ def test_make_inputs_scale_b():
 
 
 # ---------------------------------------------------------------- timing
-def test_timing_config_rules_and_stats():
+def test_timing_protocol_rules_and_stats():
     with pytest.raises(ValueError):
-        timing.TimingConfig(cache_mode="cold", batch=4)
+        timing.Protocol(mode="cold", burst=4)
     with pytest.raises(ValueError):
-        timing.TimingConfig(cache_mode="warm")
-    s = timing.summarize([10.0, 11.0, 9.0, 10.0])
-    assert s["median_us"] == 10.0 and s["n_samples"] == 4 and s["rse"] < 0.1
-    r1 = timing.TimingResult(**timing.summarize([1, 2, 3]), cache_mode="cold", batch=1, use_graph=False, wall_s=1,
-                             samples_us=[1, 2, 3])
-    r2 = timing.TimingResult(**timing.summarize([4, 5]), cache_mode="cold", batch=1, use_graph=False, wall_s=2,
-                             samples_us=[4, 5])
-    p = timing.pool([r1, r2])
-    assert p.n_samples == 5 and p.median_us == 3 and p.wall_s == 3
-    cold, graph = timing.short_configs()
-    assert cold.max_reps == 10 and graph.use_graph and graph.batch == 20
+        timing.Protocol(mode="warm")
+    with pytest.raises(ValueError):
+        timing.Protocol(samples=5, max_samples=4)
+    d = timing.describe([10.0, 11.0, 9.0, 10.0])
+    assert d["median_us"] == 10.0 and d["n"] == 4 and d["min_us"] == 9.0
+    # trimmed mean drops the outer 20 % on each side
+    assert timing.describe([1.0] * 8 + [100.0, 100.0])["trimmed_us"] == 1.0
+    r1 = timing.Timing(**timing.describe([1, 2, 3]), converged=True, mode="cold", burst=1, wall_s=1,
+                       samples_us=[1, 2, 3])
+    r2 = timing.Timing(**timing.describe([4, 5]), converged=False, mode="cold", burst=1, wall_s=2, samples_us=[4, 5])
+    m = timing.merge([r1, r2])
+    assert m.n == 5 and m.median_us == 3 and m.wall_s == 3 and not m.converged
+    assert timing.SHORT_COLD.max_samples == 10 and timing.SHORT_BURST.burst == 20 and timing.SHORT_BURST.mode == "hot"
+
+
+def test_median_ci_is_distribution_free_and_shrinks():
+    """The order-statistic interval covers the true median of a skewed distribution at about the nominal rate, and
+    narrows like 1/sqrt(n)."""
+    rng = np.random.default_rng(0)
+    true_med = math.log(2.0)  # median of Exp(1)
+    hits = 0
+    for _ in range(400):
+        x = np.sort(rng.exponential(1.0, 101))
+        lo, hi = timing.median_ci(x)
+        hits += lo <= true_med <= hi
+    assert 0.92 <= hits / 400 <= 0.99
+    w = [np.diff(timing.median_ci(np.sort(rng.exponential(1.0, n))))[0] for n in (100, 1600)]
+    assert w[1] < w[0] / 2.5
 
 
 # ---------------------------------------------------------------- winner cache
@@ -194,9 +211,9 @@ def test_choose_and_policy():
              {"config_key": "c", "valid": False}]
     assert choose(cands)["key"] == "b" and choose(cands)["mode"] == "cold"
     assert choose(cands, k=1)["key"] == "a"
-    small = [{"config_key": "a", "valid": True, "cold_us": 20.0, "graph_us": 9.0},
-             {"config_key": "b", "valid": True, "cold_us": 19.0, "graph_us": 10.0}]
-    assert choose(small)["key"] == "a" and choose(small)["mode"] == "graph"
+    small = [{"config_key": "a", "valid": True, "cold_us": 20.0, "burst_us": 9.0},
+             {"config_key": "b", "valid": True, "cold_us": 19.0, "burst_us": 10.0}]
+    assert choose(small)["key"] == "a" and choose(small)["mode"] == "burst"
     assert choose([{"config_key": "x", "valid": False}])["key"] is None
     assert KPolicy().k_for() == 3 and KPolicy().k_for(calls=2_000_000) == 5 and KPolicy().k_for(frequent=True) == 5
 
@@ -283,3 +300,16 @@ def test_placed_inputs_keep_values_and_alignment():
         seen |= {a.data_ptr(), b.data_ptr()}
     again = placed_inputs(64, 48, 80, torch.float16, seed=3, placement=2, device="cpu")
     assert torch.equal(again[0], a0)  # deterministic values for a given (seed, placement)
+
+
+def test_zero_search_rule_always_names_a_runnable_config():
+    """The rule's config passes the library's own checks (shared-memory ring, tile and split rules) for skinny,
+    square and wide shapes alike."""
+    from cs464_b200.matmul import check_config
+    from cs464_b200.select import heuristic_config
+    for M in (1, 8, 16, 24, 32, 40, 56, 64, 72, 256, 1024, 8192):
+        for N in (16, 136, 1000, 4096, 28672):
+            for K in (16, 152, 4096, 14336):
+                cfg = heuristic_config(M, N, K)
+                assert check_config(cfg, M, N, K) is None, (M, N, K, cfg.key())
+

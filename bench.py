@@ -13,11 +13,13 @@ inputs (cs464_b200.search.measure / choose), the fastest kept; `--config KEY` fo
 
 With N > 1 (torchrun, one process per GPU) every rank runs the whole sweep on its own GPU: a GEMM does not shard,
 so the ranks are replicas ("scaling": "weak"); the process group only carries the barrier and the max-reduction
-of the timings.
+of the timings. What does shard is the selector search: the `search` object of the line is BASELINE config 5's
+sharded search on a fixed 48-shape subset, the same shapes at every N, so its shapes_per_s across N is the search's
+strong scaling.
 
 `--impl reference` times the reference's CPU path for the same metric: the fp32 `a.float() @ b.float()` of
 tune/correctness.py:100-102 (the CPU oracle's restatement, oracle.reference_cpu) on the host cores, all threads,
-over a bounded sample of the sweep (sizes up to 2048 per step).
+over a bounded sample of the sweep (every size, as a block of at most 2048 rows of A against the whole B).
 """
 from __future__ import annotations
 
@@ -37,7 +39,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 SIZES = [256, 512, 1024, 2048, 4096, 8192, 16384]
-CPU_SAMPLE_SIZES = [256, 512, 1024, 2048]
+CPU_SAMPLE_ROWS = 2048   # the CPU legs time every size on a block of at most this many rows of A (the rate is
+                         # what is compared; a 16384^3 fp32 GEMM alone takes seconds on the host)
+SEARCH_SHAPES = 48       # sharded-search leg: the first 48 shapes of BASELINE config 5 at every N
+SEARCH_SPACE = 96
 METRIC = "fp16 GEMM TFLOP/s (% of B200 dense peak)"
 UNIT = "TFLOP/s"
 FALLBACK_PEAK_TFLOPS = 1590.0
@@ -57,6 +62,11 @@ def parse_args():
     ap.add_argument("--config", type=str, default=None, help="force one config key for every size")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-search", action="store_true")
+    ap.add_argument("--search-shapes", type=int, default=SEARCH_SHAPES,
+                    help="first N shapes of BASELINE config 5 for the sharded-search leg")
+    ap.add_argument("--search-space", type=int, default=SEARCH_SPACE,
+                    help="configs screened per shape (strided over the shape-pruned space), plus the ranker's top 3")
     a = ap.parse_args()
     if a.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -124,15 +134,19 @@ class ClockSampler:
 
 
 def cpu_reference(sizes, steps: int, warmup: int, budget_s: float | None = None):
-    """The reference's CPU path (fp32 matmul of the upcast fp16 inputs, all host threads) over `sizes` per step.
-    Returns (TFLOP/s, seconds per step, threads, sample description)."""
+    """The reference's CPU path (fp32 matmul of the upcast fp16 inputs, all host threads) over every size per step:
+    for size n, a block of min(n, CPU_SAMPLE_ROWS) rows of A against the whole B (a row block runs at the rate of the
+    whole GEMM; the sample keeps a step near a second). Returns (TFLOP/s, seconds per step, threads, sample)."""
     import torch
 
     from oracle import oracle
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    inputs = [oracle.make_inputs(n, n, n, seed=0) for n in sizes]
-    flops = sum(2.0 * n ** 3 for n in sizes)
+    inputs = []
+    for n in sizes:
+        a, b = oracle.make_inputs(n, n, n, seed=0)
+        inputs.append((a[:min(n, CPU_SAMPLE_ROWS)], b))
+    flops = sum(2.0 * a.shape[0] * n * n for (a, _), n in zip(inputs, sizes))
     for _ in range(warmup):
         for a, b in inputs:
             oracle.reference_cpu(a, b)
@@ -146,15 +160,16 @@ def cpu_reference(sizes, steps: int, warmup: int, budget_s: float | None = None)
         if budget_s is not None and time.perf_counter() - t_all > budget_s:
             break
     sec = statistics.median(times)
-    sample = f"square sizes {sizes} (fp16 inputs upcast to fp32, torch CPU matmul), {len(times)} timed steps"
+    sample = (f"square sizes {sizes}, each as a block of min(n, {CPU_SAMPLE_ROWS}) rows of A times the whole B (fp16 "
+              f"inputs upcast to fp32, torch CPU matmul), {len(times)} timed steps")
     return flops / sec / 1e12, sec, torch.get_num_threads(), sample
 
 
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
-    sizes = [n for n in (args.sizes_list or SIZES) if n <= max(CPU_SAMPLE_SIZES)]
-    tflops, sec, threads, sample = cpu_reference(sizes, args.steps, args.warmup)
+    sizes = args.sizes_list or SIZES
+    tflops, sec, threads, sample = cpu_reference(sizes, args.steps, min(args.warmup, 2))
     line = {"metric": METRIC, "value": round(tflops, 4), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic", "impl": "reference",
@@ -163,6 +178,47 @@ def run_reference(args, rank: int, world: int):
                              "sample": sample},
             "e2e": {"value": round(tflops, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def search_leg(args, rank: int, world: int, dev, barrier, max_over_ranks) -> dict | None:
+    """The north star's sharded selector search on a fixed subset of BASELINE config 5 (the same shapes at every N):
+    each rank claims (shape, screen slice) units from one queue in a directory on this host and searches them on its
+    own GPU (cs464_b200.shard). shapes_per_s = shapes finished / the longest rank's wall time between the start and
+    end barriers (the search is host-driven: validation, ranking and timing; no collective in between)."""
+    import torch
+    import torch.distributed as dist
+
+    from cs464_b200 import shard, suites
+    from cs464_b200.search import _ranker_default
+    shapes = suites.load("config5")[: args.search_shapes]
+    shard.limit_host_threads(shard.worker_threads(world))
+    _ranker_default()  # loaded before the timed region, as a long-lived search process has it
+    path = [tempfile.mkdtemp(prefix="b2g_search_")] if rank == 0 else [None]
+    if world > 1:
+        dist.broadcast_object_list(path, src=0)
+    out = Path(path[0])
+    queue = out / "queue.jsonl"
+    if rank == 0:
+        shard.ShapeQueue.create(queue, shapes, space=args.search_space)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    stats = shard.run_rank(rank, str(queue), str(out), str(out / "winner_cache.jsonl"), k=3,
+                           space=args.search_space, deadline_s=900.0)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    barrier()
+    wall_max = max_over_ranks(wall)
+    if rank != 0:
+        return None
+    s = shard.summarize(str(out), [{**stats, "wall_s": wall_max}], str(queue))
+    return {"workload": f"BASELINE config 5, first {len(shapes)} of its 1000 fresh shapes (seed 2): per shape the "
+                        f"ranker's top 3 (validated + short-timed: the selection) and a screen of {args.search_space} "
+                        "configs strided over the shape-pruned space plus the top 3, cold L2",
+            "shapes": s["shapes"], "units": s["units"], "ranks": world, "wall_s": round(wall_max, 3),
+            "shapes_per_s": None if s["shapes_per_s"] is None else round(s["shapes_per_s"], 4),
+            "gap_median": s["gap_median"], "gap_p95": s["gap_p95"], "crashed": s["crashed"],
+            "timing": "host wall time between barriers, max over ranks"}
 
 
 def workload_config(args) -> dict:
@@ -311,9 +367,12 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        tfl, sec, threads, sample = cpu_reference([n for n in sizes if n <= max(CPU_SAMPLE_SIZES)] or [256], 10, 3,
-                                                  budget_s=30.0)
+        tfl, sec, threads, sample = cpu_reference(sizes, 10, 1, budget_s=30.0)
         cpu = {"value": round(tfl, 4), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+
+    search = None
+    if not args.no_search:
+        search = search_leg(args, rank, world, dev, barrier, max_over_ranks)
 
     if world > 1:
         dist.barrier()
@@ -332,7 +391,7 @@ def main():
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": f"b2g::gemm_kernel at {work[dom]['n']}^3 ({work[dom]['cfg'].key()})",
                      "peak_source": peak_src},
-        "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": launches, "clocks": clocks,
+        "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": launches, "clocks": clocks, "search": search,
     }
     print(json.dumps(line), flush=True)
 

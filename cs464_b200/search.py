@@ -3,7 +3,7 @@
 Mirrors the reference's callers of its GEMM family:
   * `candidates_for(spec, M, N, K)`: backend spec strings -> `Candidate`s (tune/runner.py:42-142); specs here:
     `b200:handpicked`, `b200:heuristic`, `b200:rank[:k]`, `b200:space[:n]`, `b200:<config key>`, `torch` (B1).
-  * `measure`: validate, then short-time each candidate on one placement; a graph-amortised pass when the fastest
+  * `measure`: validate, then short-time each candidate on one placement; a burst-amortised pass when the fastest
     cold time is under 50 us; optional reverse-order confirmation (tune/online.py:244-329).
   * `choose` (tune/online.py:125-138), `search_shape` (:332-363), `select_kernel` with the winner cache and the
     call-count k policy (:58-77, :379-483).
@@ -23,7 +23,7 @@ from cs464_b200.config_space import HANDPICKED, HwLimits, full_space, prune, sha
 from cs464_b200.gate import ContextPoisoned, context_poisoned, make_inputs, reference, validate
 from cs464_b200.keys import parse_key
 from cs464_b200.matmul import B200Matmul, MatmulConfig
-from cs464_b200.timing import SMALL_US, TimingConfig, benchmark, short_configs
+from cs464_b200.timing import SHORT_BURST, SHORT_COLD, SMALL_US, Protocol, measure_us
 
 FAMILY = B200Matmul.family
 DTYPE_NAMES = {torch.float16: "fp16", torch.bfloat16: "bf16"}
@@ -132,16 +132,23 @@ def candidates_for(spec: str, M: int, N: int, K: int, prune_shapes: bool = False
 
 
 def measure(M: int, N: int, K: int, dtype, backends: list[tuple], *, inputs=None, confirm: int = 0,
-            norm_rel: bool = True) -> dict:
-    """Validate then short-time each (family, key, backend) on one placement; returns {"candidates": [...]}."""
+            norm_rel: bool = True, skip=(), on_config=None) -> dict:
+    """Validate then short-time each (family, key, backend) on one placement; returns {"candidates": [...]}.
+    Keys in `skip` (configs that crashed an earlier process on this shape) are recorded invalid without running;
+    `on_config(key)` is called before each candidate runs (the sharded search's in-flight record)."""
     if inputs is None:
         a, b = make_inputs(M, N, K, dtype)
         ref = reference(a, b)
     else:
         a, b, ref = inputs
-    cold_cfg, graph_cfg = short_configs()
     cands, bk = [], {}
     for family, key, backend in backends:
+        if key in skip:
+            cands.append({"config_key": key, "family": family, "valid": False, "failure_reason": "crashed",
+                          "setup_s": 0.0})
+            continue
+        if on_config is not None:
+            on_config(key)
         t = time.perf_counter()
         chk = validate(backend, M, N, K, dtype, ref=ref, inputs=(a, b), norm_rel=norm_rel)
         if context_poisoned(chk.failure_reason):
@@ -151,7 +158,7 @@ def measure(M: int, N: int, K: int, dtype, backends: list[tuple], *, inputs=None
              "setup_s": time.perf_counter() - t}
         if chk.valid:
             t = time.perf_counter()
-            x["cold_us"] = benchmark(backend.make_runner(a, b), cold_cfg).median_us
+            x["cold_us"] = measure_us(backend.make_runner(a, b), SHORT_COLD, keep_samples=False).median_us
             x["time_s"] = time.perf_counter() - t
         cands.append(x)
         bk[key] = backend
@@ -159,14 +166,16 @@ def measure(M: int, N: int, K: int, dtype, backends: list[tuple], *, inputs=None
     if ok and min(x["cold_us"] for x in ok) < SMALL_US:
         for x in ok:
             t = time.perf_counter()
-            x["graph_us"] = benchmark(bk[x["config_key"]].make_runner(a, b), graph_cfg).median_us
+            x["burst_us"] = measure_us(bk[x["config_key"]].make_runner(a, b), SHORT_BURST,
+                                       keep_samples=False).median_us
             x["time_s"] += time.perf_counter() - t
     if confirm > 0 and ok:
-        small = all("graph_us" in x for x in ok)
-        metric = "graph_us" if small else "cold_us"
+        small = all("burst_us" in x for x in ok)
+        metric = "burst_us" if small else "cold_us"
         for x in reversed(sorted(ok, key=lambda x: x[metric])[:confirm]):
             t = time.perf_counter()
-            again = benchmark(bk[x["config_key"]].make_runner(a, b), graph_cfg if small else cold_cfg).median_us
+            again = measure_us(bk[x["config_key"]].make_runner(a, b), SHORT_BURST if small else SHORT_COLD,
+                               keep_samples=False).median_us
             x["confirm_us"] = 0.5 * (x[metric] + again)
             x["time_s"] += time.perf_counter() - t
         for x in ok:
@@ -175,18 +184,18 @@ def measure(M: int, N: int, K: int, dtype, backends: list[tuple], *, inputs=None
 
 
 def choose(cands: list[dict], k: int | None = None) -> dict:
-    """Fastest valid candidate among the first k (all for None): by graph time when every valid candidate has one
+    """Fastest valid candidate among the first k (all for None): by burst time when every valid candidate has one
     (the fastest cold time was under 50 us), else by cold time; `confirm_us` overrides when present."""
     c = cands if k is None else cands[:k]
     ok = [x for x in c if x["valid"] and x.get("cold_us") is not None]
     cost = {"setup_s": sum(x.get("setup_s", 0.0) for x in c), "time_s": sum(x.get("time_s", 0.0) for x in c)}
     if not ok:
         return {"key": None, "mode": None, **cost}
-    small = all(x.get("graph_us") is not None for x in ok) and min(x["cold_us"] for x in ok) < SMALL_US
-    metric = "graph_us" if small else "cold_us"
+    small = all(x.get("burst_us") is not None for x in ok) and min(x["cold_us"] for x in ok) < SMALL_US
+    metric = "burst_us" if small else "cold_us"
     best = min(ok, key=lambda x: x.get("confirm_us", x[metric]))
     return {"key": best["config_key"], "family": best.get("family", FAMILY), "rank": c.index(best),
-            "mode": "graph" if small else "cold", "us": best.get("confirm_us", best[metric]), **cost}
+            "mode": "burst" if small else "cold", "us": best.get("confirm_us", best[metric]), **cost}
 
 
 def search_shape(ranker, M: int, N: int, K: int, k: int, dtype=torch.float16, order: str = "diverse",
@@ -245,11 +254,12 @@ def select_kernel(ranker, M: int, N: int, K: int, *, calls: int | None = None, f
 
 def screen_shape(M: int, N: int, K: int, configs: list[MatmulConfig] | None = None, dtype=torch.float16, *,
                  slow_factor: float = SLOW_FACTOR, samples: int = SCREEN_SAMPLES, inputs=None,
-                 log=None) -> dict:
+                 log=None, skip=(), on_config=None) -> dict:
     """Time every config (default: the shape-pruned space) with early cut-off. Each config: validate; one cold sample
     (its median of `1` after warm-up); cut as "slow" if above slow_factor x the best so far; else `samples` cold samples,
     summarised by their trimmed mean: per-launch event timestamps on this GPU fall on a ~1 us grid, so the median of a
     few samples of a 10 us kernel moves in 10 % steps, while the mean of the middle samples resolves finer.
+    Keys in `skip` are recorded "invalid: crashed" without running; `on_config(key)` runs before each config.
     Returns {"rows": [{key, status, us, n}], "best_key", "best_us", "n_configs", "wall_s"}."""
     t0 = time.perf_counter()
     cfgs = configs if configs is not None else shape_space(M, N, K)
@@ -258,12 +268,15 @@ def screen_shape(M: int, N: int, K: int, configs: list[MatmulConfig] | None = No
         ref = reference(a, b)
     else:
         a, b, ref = inputs
-    one = TimingConfig(cache_mode="cold", warmup_ms=1.0, min_warmup_iters=1, min_reps=1, max_reps=1, target_rse=1.0,
-                       max_time_s=1.0, keep_raw=False)
-    more = TimingConfig(cache_mode="cold", warmup_ms=0.0, min_warmup_iters=1, min_reps=samples, max_reps=samples,
-                        target_rse=1.0, max_time_s=2.0, keep_raw=False)
+    one = Protocol(mode="cold", samples=1, max_samples=1, warmup=1, ci_target=math.inf, max_s=1.0)
+    more = Protocol(mode="cold", samples=samples, max_samples=samples, warmup=0, ci_target=math.inf, max_s=2.0)
     rows, best = [], math.inf
     for c in cfgs:
+        if c.key() in skip:
+            rows.append({"key": c.key(), "status": "invalid: crashed", "us": None, "n": 0})
+            continue
+        if on_config is not None:
+            on_config(c.key())
         be = B200Matmul(c)
         chk = validate(be, M, N, K, dtype, ref=ref, inputs=(a, b), norm_rel=True)
         if context_poisoned(chk.failure_reason):
@@ -272,11 +285,11 @@ def screen_shape(M: int, N: int, K: int, configs: list[MatmulConfig] | None = No
             rows.append({"key": c.key(), "status": f"invalid: {chk.failure_reason}", "us": None, "n": 0})
             continue
         run = be.make_runner(a, b)
-        us = benchmark(run, one).median_us
+        us = measure_us(run, one, keep_samples=False).median_us
         if us > slow_factor * best:
             rows.append({"key": c.key(), "status": "slow", "us": us, "n": 1})
             continue
-        us = benchmark(run, more).trimmed_mean_us
+        us = measure_us(run, more, keep_samples=False).trimmed_us
         best = min(best, us)
         rows.append({"key": c.key(), "status": "ok", "us": us, "n": samples})
         if log:

@@ -29,7 +29,7 @@ EXPORTS = (
     "b2g_abi_version", "b2g_version", "b2g_source_hash", "b2g_last_error", "b2g_error_string", "b2g_status_string",
     "b2g_check", "b2g_workspace_size", "b2g_smem_bytes", "b2g_plan_create", "b2g_plan_launch",
     "b2g_plan_num_kernels", "b2g_plan_grid", "b2g_plan_destroy", "b2g_gemm", "b2g_splitk_reduce",
-    "b2g_gemm_noalloc",
+    "b2g_gemm_noalloc", "b2g_host_flag_create", "b2g_host_flag_set", "b2g_host_flag_destroy", "b2g_hold",
 )
 
 
@@ -37,7 +37,7 @@ class Config(ctypes.Structure):
     _fields_ = [("block_m", ctypes.c_int32), ("block_n", ctypes.c_int32), ("block_k", ctypes.c_int32),
                 ("num_warps", ctypes.c_int32), ("num_stages", ctypes.c_int32), ("group_m", ctypes.c_int32),
                 ("split_k", ctypes.c_int32), ("schedule", ctypes.c_int32), ("cluster", ctypes.c_int32),
-                ("reserved", ctypes.c_int32 * 7)]
+                ("wait_limit_us", ctypes.c_int32), ("reserved", ctypes.c_int32 * 6)]
 
 
 class Problem(ctypes.Structure):
@@ -88,6 +88,10 @@ def _declare(lib: ctypes.CDLL) -> None:
         "b2g_splitk_reduce": (c_int32, [c_void_p, c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                         ctypes.c_int64, c_int32, c_int32, c_void_p]),
         "b2g_gemm_noalloc": (c_int32, [P(Config), P(Problem), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+        "b2g_host_flag_create": (c_int32, [P(c_void_p), P(c_void_p)]),
+        "b2g_host_flag_set": (c_int32, [c_void_p, c_int32]),
+        "b2g_host_flag_destroy": (c_int32, [c_void_p]),
+        "b2g_hold": (c_int32, [c_void_p, c_int32, ctypes.c_uint64, c_void_p, c_void_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

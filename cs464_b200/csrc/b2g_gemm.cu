@@ -619,6 +619,27 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     };
     const int64_t slot_elems = static_cast<int64_t>(p.cta_m) * p.tile_n;
     float* const my_slot = p.streamk ? p.sk_slots + static_cast<int64_t>(blockIdx.x) * slot_elems : nullptr;
+    // Stream-K owner: add the fp32 partials that contributors j0 .. j1-1 (later K blocks, in worker order) left for
+    // `ncol` columns at offset `off` of their slots, in that fixed order.
+    auto add_partials = [&](uint32_t (&v)[32], int64_t off, int ncol, int j0, int j1) {
+      for (int j = j0; j < j1; ++j) {
+        const float4* src = reinterpret_cast<const float4*>(
+            p.sk_slots + static_cast<int64_t>(PAIR ? 2 * j + static_cast<int>(rank) : j) * slot_elems + off);
+        float4 x[8];
+#pragma unroll
+        for (int k4 = 0; k4 < 8; ++k4)
+          if (k4 * 4 < ncol) x[k4] = src[k4];
+#pragma unroll
+        for (int k4 = 0; k4 < 8; ++k4) {
+          if (k4 * 4 < ncol) {
+            v[4 * k4] = __float_as_uint(__uint_as_float(v[4 * k4]) + x[k4].x);
+            v[4 * k4 + 1] = __float_as_uint(__uint_as_float(v[4 * k4 + 1]) + x[k4].y);
+            v[4 * k4 + 2] = __float_as_uint(__uint_as_float(v[4 * k4 + 2]) + x[k4].z);
+            v[4 * k4 + 3] = __float_as_uint(__uint_as_float(v[4 * k4 + 3]) + x[k4].w);
+          }
+        }
+      }
+    };
     Cursor ec;
     cursor_init(p, ec, first_unit, unit_step);
     Unit w;
@@ -659,7 +680,7 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
         if (row0 >= p.rows_a) break;
         const int64_t row = row0 + lane;
         const int row_local = h * 128 + q * 32 + lane;  // row within this CTA's part of the tile
-        if (p.stage_c && !contrib && !owner) {
+        if (p.stage_c && !contrib) {
           const uint32_t stg = data + p.epi_stage_off + static_cast<uint32_t>(e) * 4096u;
           const int rows_in = p.rows_a - row0 < 32 ? static_cast<int>(p.rows_a - row0) : 32;
           if (p.out_kind == OUT_F32_PARTIAL) {  // 32 fp32 columns per 128-byte row
@@ -706,6 +727,9 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
                                  v);
                   tmem_ld_wait();
                 }
+                if (owner)
+                  add_partials(v, static_cast<int64_t>(row_local) * p.tile_n + c2 * 64 + hh * 32, 32, first_unit + 1,
+                               j_end);
                 uint4 pc[4];
 #pragma unroll
                 for (int k4 = 0; k4 < 4; ++k4) {
@@ -750,26 +774,7 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
             }
             continue;
           }
-          if (owner) {  // add the contributors' partials in K order (the hybrid schedule keeps them few)
-            for (int j = first_unit + 1; j < j_end; ++j) {
-              const float4* src = reinterpret_cast<const float4*>(
-                  p.sk_slots + static_cast<int64_t>(PAIR ? 2 * j + static_cast<int>(rank) : j) * slot_elems +
-                  slot_off);
-              float4 x[8];
-#pragma unroll
-              for (int k4 = 0; k4 < 8; ++k4)
-                if (k4 * 4 < ncol) x[k4] = src[k4];
-#pragma unroll
-              for (int k4 = 0; k4 < 8; ++k4) {
-                if (k4 * 4 < ncol) {
-                  v[4 * k4] = __float_as_uint(__uint_as_float(v[4 * k4]) + x[k4].x);
-                  v[4 * k4 + 1] = __float_as_uint(__uint_as_float(v[4 * k4 + 1]) + x[k4].y);
-                  v[4 * k4 + 2] = __float_as_uint(__uint_as_float(v[4 * k4 + 2]) + x[k4].z);
-                  v[4 * k4 + 3] = __float_as_uint(__uint_as_float(v[4 * k4 + 3]) + x[k4].w);
-                }
-              }
-            }
-          }
+          if (owner) add_partials(v, slot_off, ncol, first_unit + 1, j_end);  // contributors' partials, K order
           store_chunk(p, w.split, row, static_cast<int64_t>(w.tn) * p.tile_n + c * 32, ncol, v);
         }
       }
@@ -867,13 +872,20 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* __restr
 using namespace b2g;
 
 namespace {
-
 thread_local std::string g_last_error;
+}  // namespace
 
-int32_t fail(int32_t code, const std::string& msg) {
+namespace b2g {
+// The message b2g_last_error() returns on this thread (the timing helpers in b2g_timing.cu report through it too).
+int32_t record_error(int32_t code, const std::string& msg) {
   g_last_error = msg;
   return code;
 }
+}  // namespace b2g
+
+namespace {
+
+int32_t fail(int32_t code, const std::string& msg) { return record_error(code, msg); }
 
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
@@ -1021,6 +1033,11 @@ int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g,
     return fail(B2G_ERR_UNSUPPORTED, "schedule_invalid");
   if (cfg->schedule == B2G_SCHED_STREAMK && cfg->split_k != 1)
     return fail(B2G_ERR_UNSUPPORTED, "streamk_with_split_k: stream-K balances K itself; SPLIT_K must be 1");
+  if (cfg->wait_limit_us < 0) return fail(B2G_ERR_INVALID_ARG, "wait_limit_us must be >= 0");
+  if (cfg->wait_limit_us > 0 && g.pair)
+    return fail(B2G_ERR_UNSUPPORTED,
+                "wait_limit_single_cta_only: a CTA pair keeps the default wait limit (an early stop cannot wait out "
+                "the second CTA's copies)");
   g.streamk = cfg->schedule == B2G_SCHED_STREAMK;
   g.bk = bk;
   g.stages = cfg->num_stages;
@@ -1082,6 +1099,12 @@ int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g,
     g.sk_slots_off = static_cast<size_t>(round_up(g.sk_max_ctas * 4, 256));
     sk_bytes = g.sk_slots_off +
                static_cast<size_t>(round_up(g.sk_max_ctas * static_cast<int64_t>(g.cta_m) * g.tile_n * 4, 256));
+  }
+  if (K == 0) {
+    // An empty K only zero-fills C: no GEMM launch, so no partials, fix-up state or staged operands are needed.
+    g.ws_partial = 0;
+    sk_bytes = 0;
+    g.a.pack = g.b.pack = 0;
   }
   g.a.ws_off = g.ws_partial + sk_bytes;
   g.b.ws_off = g.a.ws_off + packed_bytes(g.a);
@@ -1307,7 +1330,7 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
     k.num_acc = g.num_acc;
     k.tmem_cols = g.tmem_cols;
     k.status = status;
-    k.timeout_ns = kWaitTimeoutNs;
+    k.timeout_ns = cfg->wait_limit_us > 0 ? static_cast<uint64_t>(cfg->wait_limit_us) * 1000ull : kWaitTimeoutNs;
     k.streamk = g.streamk;
     k.sk_dp_tiles = 0;
     k.sk_workers = 1;
@@ -1350,7 +1373,7 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
       const size_t staging = static_cast<size_t>(g.epi_warps) * 4096;
       const bool partial = cfg->split_k > 1;
       const bool pieces_ok = partial ? (N % 4 == 0) : (N % 8 == 0 && g.tile_n % 64 == 0);
-      if (!g.swapped && !g.streamk && k.vec_ok && pieces_ok && g.smem + staging <= kMaxSmemPerCta) {
+      if (!g.swapped && k.vec_ok && pieces_ok && g.smem + staging <= kMaxSmemPerCta) {
         k.stage_c = 1;
         k.epi_stage_off = static_cast<uint32_t>(static_cast<size_t>(g.cta_m + g.cta_n) * g.bk * 2 * g.stages);
         p->smem = g.smem + staging;
@@ -1388,17 +1411,31 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
       }
       grid = std::min<int64_t>(grid, slots);
       if (g.streamk) {
-        // Every worker resident at once (owners wait for contributors). Whole waves of tiles run data-parallel; the
-        // last one or two waves' tiles are shared in K, by at most as many workers as keep a slice of
-        // max(4, num_kb / 4) K blocks each, so a tile is split a few ways, not per worker.
+        // Every worker resident at once (owners wait for contributors). Two policies, by the last wave's fill:
+        //  * the tiles of the partial last wave (r of them) fit at least twice into the workers: every full wave runs
+        //    data-parallel and each of the r tiles is split evenly over s = workers / r workers in K, so the last
+        //    wave takes 1/s of a tile's time (plus one fix-up) instead of a whole one;
+        //  * otherwise (a last wave more than half full): whole waves minus one run data-parallel and the rest is
+        //    shared in K by all workers, in slices of at least max(4, num_kb / 4) K blocks.
         const int64_t tiles = static_cast<int64_t>(g.tiles_m) * g.tiles_n;
         grid = std::min<int64_t>(slots, std::max<int64_t>(tiles, 1) * g.num_kb);
         if (grid * (g.pair ? 2 : 1) > g.sk_max_ctas) grid = g.sk_max_ctas / (g.pair ? 2 : 1);
         grid = std::max<int64_t>(grid, 1);
-        const int64_t dp_tiles = std::max<int64_t>(0, tiles / grid - 1) * grid;
-        const int64_t iters = (tiles - dp_tiles) * g.num_kb;
         const int64_t min_slice = std::max<int64_t>(4, g.num_kb / 4);
-        const int64_t workers = std::max<int64_t>(1, std::min<int64_t>(grid, iters / min_slice));
+        const int64_t full = tiles / grid, r = tiles % grid;
+        const int64_t split = r > 0 ? std::min<int64_t>(grid / r, std::max<int64_t>(1, g.num_kb / min_slice)) : 0;
+        int64_t dp_tiles, workers;
+        if (r == 0) {  // whole waves: nothing to share
+          dp_tiles = tiles;
+          workers = 1;
+        } else if (split >= 2) {
+          dp_tiles = full * grid;
+          workers = r * split;
+        } else {
+          dp_tiles = std::max<int64_t>(0, full - 1) * grid;
+          workers = std::max<int64_t>(1, std::min<int64_t>(grid, (tiles - dp_tiles) * g.num_kb / min_slice));
+        }
+        const int64_t iters = (tiles - dp_tiles) * g.num_kb;
         p->kp.sk_dp_tiles = static_cast<int32_t>(dp_tiles);
         p->kp.sk_iters = iters;
         p->kp.sk_workers = static_cast<int32_t>(workers);
@@ -1463,6 +1500,7 @@ const char* b2g_status_string(int32_t status) {
     case kStatusMmaTimeout: return "device wait timed out in the MMA issuer";
     case kStatusEpilogueTimeout: return "device wait timed out in the epilogue";
     case kStatusStreamkTimeout: return "stream-K owner timed out waiting for a contributor's partial";
+    case 0x201: return "timing gate released by its time limit, not by the host";
     default: return "unknown device status";
   }
 }

@@ -154,8 +154,11 @@ class B200Matmul:
 
     family = "b200_sm100a_v1"
 
-    def __init__(self, cfg: MatmulConfig | dict):
+    def __init__(self, cfg: MatmulConfig | dict, wait_limit_us: int = 0):
+        """`wait_limit_us`: limit of the kernels' bounded device waits (0: the library's default of one second);
+        single-CTA configs only. Not part of the config's identity."""
         self.cfg = cfg if isinstance(cfg, MatmulConfig) else MatmulConfig.from_dict(cfg)
+        self.wait_limit_us = int(wait_limit_us)
 
     @property
     def key(self) -> str:
@@ -176,6 +179,7 @@ class B200Matmul:
         lib = _abi.load()
         pr = problem(M, N, K, a.stride(), b.stride(), c.stride(), a.dtype)
         acfg = cfg.to_abi()
+        acfg.wait_limit_us = self.wait_limit_us
         n = ctypes.c_size_t(0)
         with torch.cuda.device(dev):
             _abi.check(lib.b2g_workspace_size(ctypes.byref(acfg), ctypes.byref(pr), a.data_ptr(), b.data_ptr(),

@@ -9,6 +9,8 @@ from __future__ import annotations
 from cs464_b200.matmul import MatmulConfig
 
 SM_COUNT = 148
+SMEM_BYTES = 232448   # opt-in dynamic shared memory per block on sm_100
+CTL_BYTES = 2048      # the kernel's control block and alignment slack in front of the ring
 
 
 def heuristic_config(M: int, N: int, K: int, sm_count: int = SM_COUNT) -> MatmulConfig:
@@ -20,9 +22,14 @@ def heuristic_config(M: int, N: int, K: int, sm_count: int = SM_COUNT) -> Matmul
         split = 1
         while tiles * split < sm_count and split * 2 <= 16 and kb // (split * 2) >= 4:
             split *= 2
-        stages = 6 if bm <= 32 else 5
+        # the deepest ring (up to 6) whose stages of 128 B-rows + bm A-rows x 128 K fit the shared memory
+        stages = min(6, (SMEM_BYTES - CTL_BYTES) // ((128 + bm) * 128 * 2))
         return MatmulConfig(bm, 128, 128, num_warps=4, num_stages=stages, GROUP_M=1, SPLIT_K=split)
     tiles_big = -(-M // 256) * -(-N // 256)
+    if tiles_big >= sm_count:
+        # several waves of 256 x 256 tiles: a CTA pair per tile (half the B operand per SM, double-buffered
+        # accumulators), K step 128: the fastest large-shape family member measured on B200
+        return MatmulConfig(256, 256, 128, num_warps=4, num_stages=3, GROUP_M=8, CLUSTER=2)
     if tiles_big >= sm_count // 2:
         return MatmulConfig(256, 256, 64, num_warps=4, num_stages=3, GROUP_M=8)
     tiles = -(-M // 128) * -(-N // 128)

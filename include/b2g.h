@@ -66,7 +66,12 @@ typedef struct b2g_config {
   int32_t split_k;
   int32_t schedule; /* B2G_SCHED_* */
   int32_t cluster;  /* 1: one CTA per tile; 2: a CTA pair per tile */
-  int32_t reserved[7];
+  /* Limit of every bounded device-side wait, in microseconds; 0 selects the default of one second. A wait that runs
+     out writes its code to the status word and the kernel stops early (C is then incomplete). Single-CTA variants
+     only: with cluster = 2 a non-zero value is B2G_ERR_UNSUPPORTED, because a pair that stops early cannot wait out
+     the copies its second CTA already issued. */
+  int32_t wait_limit_us;
+  int32_t reserved[6];
 } b2g_config;
 
 /*
@@ -135,6 +140,18 @@ int32_t b2g_gemm(const b2g_config* cfg, const b2g_problem* prob, const void* A, 
 int32_t b2g_splitk_reduce(const float* ws, void* C, int64_t M, int64_t N, int64_t stride_cm, int64_t stride_cn,
                           int32_t split, int32_t dtype, void* stream);
 
+/* ---- timing support (the candidate timer's stream gate; no counterpart in the reference, whose timer queues a
+   calibrated device sleep instead, tune/timing.py:151-154) ----
+   A 4-byte flag in mapped, pinned host memory: *host_ptr for the host, *device_ptr for kernels. */
+int32_t b2g_host_flag_create(int32_t** host_ptr, int32_t** device_ptr);
+/* store `value` into the flag (sequentially consistent; the device sees it on its next read) */
+int32_t b2g_host_flag_set(int32_t* host_ptr, int32_t value);
+int32_t b2g_host_flag_destroy(int32_t* host_ptr);
+/* Enqueue on `stream` a one-thread kernel that returns once *device_flag == expect, so the work queued after it
+   starts only when the host sets the flag. Bounded: after timeout_ns it writes 0x201 into *status (may be NULL) and
+   returns. */
+int32_t b2g_hold(const int32_t* device_flag, int32_t expect, uint64_t timeout_ns, int32_t* status, void* stream);
+
 /* Allocation-free GEMM. It has no counterpart in the reference: the reference always allocates its split-K workspace
    with torch (kernels/triton_matmul.py:133).
    For callers that may not allocate device memory themselves: plugin hosts that hand a library only its input and
@@ -145,8 +162,9 @@ int32_t b2g_splitk_reduce(const float* ws, void* C, int64_t M, int64_t N, int64_
    on every GPU that loads the library, held until the process exits.
    Limits and rules:
    - split-K partials larger than 32 MiB (4 * SPLIT_K * M * N bytes) are rejected with B2G_ERR_WORKSPACE and a
-     message naming both sizes; operands that would need staging (unaligned bases or leading dimensions) are
-     rejected with B2G_ERR_UNSUPPORTED.
+     message naming both sizes; operands that would need staging (unaligned bases or leading dimensions) and the
+     stream-K schedule (its fix-up flags must start zeroed in a caller workspace) are rejected with
+     B2G_ERR_UNSUPPORTED. K = 0 needs no partials whatever SPLIT_K is.
    - The first call on each device looks up the scratch array's device address (cudaGetSymbolAddress) with that
      device current; make that first call before any stream capture begins.
    - All calls share the one scratch array, which keeps the contents of the last call. Nothing in it needs to start

@@ -30,6 +30,7 @@ EXPORTS = (
     "b2g_check", "b2g_workspace_size", "b2g_smem_bytes", "b2g_plan_create", "b2g_plan_launch",
     "b2g_plan_num_kernels", "b2g_plan_grid", "b2g_plan_destroy", "b2g_gemm", "b2g_splitk_reduce",
     "b2g_gemm_noalloc", "b2g_host_flag_create", "b2g_host_flag_set", "b2g_host_flag_destroy", "b2g_hold",
+    "b2g_forest_predict",
 )
 
 
@@ -92,6 +93,9 @@ def _declare(lib: ctypes.CDLL) -> None:
         "b2g_host_flag_set": (c_int32, [c_void_p, c_int32]),
         "b2g_host_flag_destroy": (c_int32, [c_void_p]),
         "b2g_hold": (c_int32, [c_void_p, c_int32, ctypes.c_uint64, c_void_p, c_void_p]),
+        "b2g_forest_predict": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_int32, ctypes.c_double, c_void_p, ctypes.c_int64, c_int32, c_void_p,
+                                         c_int32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -7,7 +7,8 @@ the ranker interface (`rank(M, N, K, k, order)`, `scores`, `cfgs`, `pool_keys`, 
   * `AnalyticRanker`: a roofline model of this kernel on B200 (waves over 148 SMs, tensor time per tile, L2->SM and
     HBM bytes, per-K-step issue overhead, split-K and staging costs); needs no training data;
   * `LearnedRanker`: gradient-boosted trees (scikit-learn) over the same features, fitted on measured screens of
-    this family on B200 (`fit(rows)`), saved as <stem>.pkl + <stem>.json.
+    this family on B200 (`fit(rows)`), saved as <stem>.trees.npz (the trees as plain arrays, scored natively) +
+    <stem>.json.
 """
 from __future__ import annotations
 
@@ -229,8 +230,68 @@ class AnalyticRanker:
         return [self.pool_keys[i] for i in out]
 
 
+class Forest:
+    """A regression tree ensemble as plain arrays, scored by the library's native predictor (`b2g_forest_predict`):
+    the shipped model needs neither the training library nor its version. Node n: feature (-1 at a leaf), threshold,
+    left / right child (global node indices), missing-value direction, value; roots[t] is tree t's first node."""
+
+    FIELDS = ("feature", "threshold", "left", "right", "missing_left", "value", "roots")
+
+    def __init__(self, feature, threshold, left, right, missing_left, value, roots, base: float):
+        self.feature = np.ascontiguousarray(feature, dtype=np.int32)
+        self.threshold = np.ascontiguousarray(threshold, dtype=np.float64)
+        self.left = np.ascontiguousarray(left, dtype=np.int32)
+        self.right = np.ascontiguousarray(right, dtype=np.int32)
+        self.missing_left = np.ascontiguousarray(missing_left, dtype=np.uint8)
+        self.value = np.ascontiguousarray(value, dtype=np.float64)
+        self.roots = np.ascontiguousarray(roots, dtype=np.int32)
+        self.base = float(base)
+
+    @classmethod
+    def from_sklearn(cls, model) -> "Forest":
+        """Flatten a fitted scikit-learn HistGradientBoostingRegressor (numeric features, one output)."""
+        parts, roots, off = [], [], 0
+        for (pred,) in model._predictors:
+            nd = pred.nodes
+            if nd["is_categorical"].any():
+                raise ValueError("categorical splits are not supported")
+            leaf = nd["is_leaf"].astype(bool)
+            parts.append((np.where(leaf, -1, nd["feature_idx"]), nd["num_threshold"],
+                          np.where(leaf, -1, nd["left"] + off), np.where(leaf, -1, nd["right"] + off),
+                          nd["missing_go_to_left"], nd["value"]))
+            roots.append(off)
+            off += len(nd)
+        cols = [np.concatenate([p[i] for p in parts]) for i in range(6)]
+        return cls(*cols, roots, float(np.ravel(model._baseline_prediction)[0]))
+
+    def predict(self, X: np.ndarray, threads: int | None = None) -> np.ndarray:
+        import ctypes
+        import os
+
+        from cs464_b200 import _abi
+        X = np.ascontiguousarray(X, dtype=np.float64)
+        out = np.empty(X.shape[0], dtype=np.float64)
+        ptr = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+        n_threads = threads or int(os.environ.get("OMP_NUM_THREADS") or os.cpu_count() or 1)
+        rc = _abi.load().b2g_forest_predict(ptr(self.feature), ptr(self.threshold), ptr(self.left), ptr(self.right),
+                                            ptr(self.missing_left), ptr(self.value), ptr(self.roots),
+                                            len(self.roots), self.base, ptr(X), X.shape[0], X.shape[1], ptr(out),
+                                            n_threads)
+        _abi.check(rc, "b2g_forest_predict")
+        return out
+
+    def save(self, path: str | Path) -> None:
+        np.savez_compressed(path, base=np.array([self.base]), **{f: getattr(self, f) for f in self.FIELDS})
+
+    @classmethod
+    def load(cls, path: str | Path) -> "Forest":
+        z = np.load(path)
+        return cls(*(z[f] for f in cls.FIELDS), float(z["base"][0]))
+
+
 class LearnedRanker(AnalyticRanker):
-    """Gradient-boosted trees over `candidate_features`, predicting log(time / best time of the shape)."""
+    """Gradient-boosted trees over `candidate_features`, predicting log(time / best time of the shape). Trained
+    with scikit-learn, stored and scored as a `Forest` (<stem>.trees.npz + <stem>.json)."""
 
     kind = "learned"
 
@@ -255,7 +316,7 @@ class LearnedRanker(AnalyticRanker):
         y = np.concatenate(ys)
         params = {"max_iter": 600, "learning_rate": 0.05, "max_leaf_nodes": 63, "random_state": 0}
         params.update(kw)
-        self.model = HistGradientBoostingRegressor(**params).fit(X, y)
+        self.model = Forest.from_sklearn(HistGradientBoostingRegressor(**params).fit(X, y))
         return self
 
     def scores(self, M: int, N: int, K: int) -> np.ndarray:
@@ -264,25 +325,19 @@ class LearnedRanker(AnalyticRanker):
         return self.model.predict(self._pool.features(M, N, K))
 
     def save(self, stem: str | Path, info: dict | None = None) -> None:
-        import pickle
         stem = Path(stem)
         stem.parent.mkdir(parents=True, exist_ok=True)
-        with open(f"{stem}.pkl", "wb") as f:
-            pickle.dump(self.model, f)
+        self.model.save(f"{stem}.trees.npz")
         Path(f"{stem}.json").write_text(json.dumps({"features": FEATURES, "info": info or {}, "pool": self.pool_keys}))
         self.stem = str(stem)
 
     @classmethod
     def load(cls, stem: str | Path) -> "LearnedRanker":
-        import pickle
-
         from cs464_b200.keys import parse_key
         meta = json.loads(Path(f"{stem}.json").read_text())
         if meta["features"] != FEATURES:
             raise ValueError(f"{stem}: feature list differs from this version's; retrain")
-        with open(f"{stem}.pkl", "rb") as f:
-            model = pickle.load(f)
-        r = cls(model, [parse_key(k) for k in meta["pool"]])
+        r = cls(Forest.load(f"{stem}.trees.npz"), [parse_key(k) for k in meta["pool"]])
         r.stem = str(stem)
         return r
 
@@ -291,9 +346,9 @@ MODEL_STEM = Path(__file__).resolve().parent / "models" / "ranker_b200"
 
 
 def default_ranker():
-    """The shipped learned ranker when its files exist (cs464_b200/models/ranker_b200.{pkl,json}), else the analytic
+    """The shipped learned ranker when its files exist (cs464_b200/models/ranker_b200.{trees.npz,json}), else the analytic
     one. A model whose feature list no longer matches this code is ignored (warned)."""
-    if Path(f"{MODEL_STEM}.pkl").exists() and Path(f"{MODEL_STEM}.json").exists():
+    if Path(f"{MODEL_STEM}.trees.npz").exists() and Path(f"{MODEL_STEM}.json").exists():
         try:
             return LearnedRanker.load(MODEL_STEM)
         except Exception as e:

@@ -152,6 +152,17 @@ int32_t b2g_host_flag_destroy(int32_t* host_ptr);
    returns. */
 int32_t b2g_hold(const int32_t* device_flag, int32_t expect, uint64_t timeout_ns, int32_t* status, void* stream);
 
+/* ---- selector support ----
+   Scores of a tree ensemble (the learned ranker's model, stored as arrays; no counterpart in the reference, which
+   calls LightGBM's own predictor, analysis/learned.py:488-516). Node n: feature[n] (-1 for a leaf), threshold[n],
+   children left[n] / right[n] (indices into the same arrays), missing_left[n] (direction of a NaN), value[n] (a
+   leaf's output). roots[t] is tree t's root. out[r] = base + sum over t in order of the leaf value row r reaches,
+   going left when X[r, feature] <= threshold. X is row-major [n_rows, n_features] double. Host only. */
+int32_t b2g_forest_predict(const int32_t* feature, const double* threshold, const int32_t* left, const int32_t* right,
+                           const uint8_t* missing_left, const double* value, const int32_t* roots, int32_t n_trees,
+                           double base, const double* X, int64_t n_rows, int32_t n_features, double* out,
+                           int32_t threads);
+
 /* Allocation-free GEMM. It has no counterpart in the reference: the reference always allocates its split-K workspace
    with torch (kernels/triton_matmul.py:133).
    For callers that may not allocate device memory themselves: plugin hosts that hand a library only its input and

@@ -186,11 +186,37 @@ def test_learned_ranker_fit_save_load(tmp_path):
                          "us": analytic_time_s(M, N, K, c) * 1e6 * float(rng.uniform(0.9, 1.1))})
     lr = LearnedRanker(pool=pool).fit(rows, max_iter=30)
     lr.save(tmp_path / "rk")
+    assert (tmp_path / "rk.trees.npz").exists() and not list(tmp_path.glob("*.pkl"))
     lr2 = LearnedRanker.load(tmp_path / "rk")
     assert lr2.pool_keys == lr.pool_keys
-    assert np.allclose(lr2.scores(512, 512, 512), lr.scores(512, 512, 512))
+    assert np.array_equal(lr2.scores(512, 512, 512), lr.scores(512, 512, 512))
     assert len(lr2.rank(512, 512, 512, 3)) == 3
     assert set(candidate_features(1, 2, 3, pool[0])) >= {"log2_M", "BLOCK_M", "waves", "log_analytic_us"}
+
+
+def test_forest_reproduces_the_training_library_bit_for_bit():
+    """The array form of a fitted tree ensemble, scored by the library's native predictor, gives exactly the
+    training library's predictions (same leaves, same summation order), NaN inputs included."""
+    from sklearn.ensemble import HistGradientBoostingRegressor
+
+    from cs464_b200.ranker import Forest
+    rng = np.random.default_rng(1)
+    X = rng.normal(size=(600, 7))
+    y = np.sin(X[:, 0]) + X[:, 1] * X[:, 2] + 0.1 * rng.normal(size=600)
+    X[rng.random(X.shape) < 0.05] = np.nan
+    m = HistGradientBoostingRegressor(max_iter=40, max_leaf_nodes=15, random_state=0).fit(X, y)
+    f = Forest.from_sklearn(m)
+    Xt = rng.normal(size=(1000, 7))
+    Xt[rng.random(Xt.shape) < 0.05] = np.nan
+    assert np.array_equal(f.predict(Xt), m.predict(Xt))
+    assert np.array_equal(f.predict(Xt, threads=1), f.predict(Xt, threads=4))
+
+
+def test_shipped_ranker_is_plain_arrays():
+    from cs464_b200 import ranker as rk
+    r = rk.default_ranker()
+    assert r.kind == "learned" and isinstance(r.model, rk.Forest)
+    assert not list(Path(rk.MODEL_STEM).parent.glob("*.pkl"))
 
 
 def test_candidates_for_specs():

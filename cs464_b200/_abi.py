@@ -30,7 +30,7 @@ EXPORTS = (
     "b2g_check", "b2g_workspace_size", "b2g_smem_bytes", "b2g_plan_create", "b2g_plan_launch",
     "b2g_plan_num_kernels", "b2g_plan_grid", "b2g_plan_destroy", "b2g_gemm", "b2g_splitk_reduce",
     "b2g_gemm_noalloc", "b2g_host_flag_create", "b2g_host_flag_set", "b2g_host_flag_destroy", "b2g_hold",
-    "b2g_forest_predict",
+    "b2g_forest_predict", "b2g_plan_rebind",
 )
 
 
@@ -81,6 +81,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "b2g_plan_create": (c_int32, [P(Config), P(Problem), c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                       c_void_p, P(c_void_p)]),
         "b2g_plan_launch": (c_int32, [c_void_p, c_void_p]),
+        "b2g_plan_rebind": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p]),
         "b2g_plan_num_kernels": (c_int32, [c_void_p]),
         "b2g_plan_grid": (c_int32, [c_void_p]),
         "b2g_plan_destroy": (c_int32, [c_void_p]),

@@ -207,22 +207,20 @@ __device__ __forceinline__ bool cursor_next(const KParams& p, Cursor& c, int wor
 
 // Bounded wait: true once the phase with `parity` completed; false if another role aborted or `timeout_ns` passed
 // (then this role sets the abort flag and records `code`).
+// The slow path suspends on the barrier in slices of at most a quarter of the limit (at most 1 ms), so the limit
+// holds to within a slice whatever the hardware's own suspend time is.
 __device__ __noinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag, int* status,
                                         uint64_t timeout_ns, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = 0;
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0) {
-      if (*abort_flag) return false;
-      const uint64_t now = global_timer_ns();
-      if (t0 == 0) {
-        t0 = now;
-      } else if (now - t0 > timeout_ns) {
-        *abort_flag = 1u;
-        if (status) atomicCAS(status, 0, code);
-        return false;
-      }
+  const uint32_t slice = static_cast<uint32_t>(timeout_ns / 4 < 1000000ull ? timeout_ns / 4 : 1000000ull);
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    if (mbar_try_wait_hint(bar, parity, slice)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > timeout_ns) {
+      *abort_flag = 1u;
+      if (status) atomicCAS(status, 0, code);
+      return false;
     }
   }
 }
@@ -625,17 +623,21 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
       for (int j = j0; j < j1; ++j) {
         const float4* src = reinterpret_cast<const float4*>(
             p.sk_slots + static_cast<int64_t>(PAIR ? 2 * j + static_cast<int>(rank) : j) * slot_elems + off);
-        float4 x[8];
 #pragma unroll
-        for (int k4 = 0; k4 < 8; ++k4)
-          if (k4 * 4 < ncol) x[k4] = src[k4];
+        for (int h4 = 0; h4 < 8; h4 += 4) {  // four 16-byte loads in flight at a time (register pressure)
+          float4 x[4];
 #pragma unroll
-        for (int k4 = 0; k4 < 8; ++k4) {
-          if (k4 * 4 < ncol) {
-            v[4 * k4] = __float_as_uint(__uint_as_float(v[4 * k4]) + x[k4].x);
-            v[4 * k4 + 1] = __float_as_uint(__uint_as_float(v[4 * k4 + 1]) + x[k4].y);
-            v[4 * k4 + 2] = __float_as_uint(__uint_as_float(v[4 * k4 + 2]) + x[k4].z);
-            v[4 * k4 + 3] = __float_as_uint(__uint_as_float(v[4 * k4 + 3]) + x[k4].w);
+          for (int k4 = 0; k4 < 4; ++k4)
+            if ((h4 + k4) * 4 < ncol) x[k4] = src[h4 + k4];
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const int e = 4 * (h4 + k4);
+            if (e < ncol) {
+              v[e] = __float_as_uint(__uint_as_float(v[e]) + x[k4].x);
+              v[e + 1] = __float_as_uint(__uint_as_float(v[e + 1]) + x[k4].y);
+              v[e + 2] = __float_as_uint(__uint_as_float(v[e + 2]) + x[k4].z);
+              v[e + 3] = __float_as_uint(__uint_as_float(v[e + 3]) + x[k4].w);
+            }
           }
         }
       }
@@ -1211,6 +1213,13 @@ struct b2g_plan {
   void* r_c;
   int64_t r_M, r_N, r_scm, r_scn;
   int r_split, r_bf16, r_vec;
+  // what b2g_plan_rebind needs: the caller's pointers, the MMA operands' layouts (MMA "A" is the caller's B when
+  // `swapped`), the element type and K step
+  const void* user_a;
+  const void* user_b;
+  void* user_c;
+  Operand op_a, op_b;
+  int swapped, dtype, bk;
 };
 
 namespace {
@@ -1444,7 +1453,21 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
     }
     p->grid = static_cast<int>(std::max<int64_t>(grid, 1));
   }
+  p->user_a = A;
+  p->user_b = B;
+  p->user_c = C;
+  p->op_a = g.a;
+  p->op_b = g.b;
+  p->swapped = g.swapped;
+  p->dtype = prob->dtype;
+  p->bk = g.bk;
   return B2G_OK;
+}
+
+// Same 16-byte (and 8-byte) alignment class: the layout decisions made for the old pointer hold for the new one.
+bool same_alignment(const void* x, const void* y) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(x), b = reinterpret_cast<uintptr_t>(y);
+  return (a & 15u) == (b & 15u);
 }
 
 // ---------------------------------------------------------------- allocation-free entry point
@@ -1617,6 +1640,58 @@ int32_t b2g_plan_launch(const b2g_plan* p, void* stream) {
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
+  return B2G_OK;
+}
+
+int32_t b2g_plan_rebind(b2g_plan* p, const void* A, const void* B, void* C) {
+  if (!p) return fail(B2G_ERR_INVALID_ARG, "null plan");
+  if (p->empty) return B2G_OK;
+  if (!C || (!p->k_zero && (!A || !B))) return fail(B2G_ERR_INVALID_ARG, "null A, B or C");
+  if (!same_alignment(A, p->user_a) || !same_alignment(B, p->user_b) || !same_alignment(C, p->user_c))
+    return fail(B2G_ERR_INVALID_ARG,
+                "rebind_alignment_changed: a pointer's 16-byte alignment differs from the plan's; create a new plan");
+  if (p->k_zero) {
+    p->r_c = C;
+    p->user_c = C;
+    return B2G_OK;
+  }
+  // MMA operand "a" reads the caller's A (or B when swapped); a staged operand keeps its workspace copy and only
+  // changes the source of the staging copy
+  const void* src_a = p->swapped ? B : A;
+  const void* src_b = p->swapped ? A : B;
+  const void* old_a = p->swapped ? p->user_b : p->user_a;
+  const void* old_b = p->swapped ? p->user_a : p->user_b;
+  CUtensorMap ta = p->tma_a, tb = p->tma_b;
+  int32_t is3d = 0;
+  if (src_a != old_a) {
+    if (p->pack_a) {
+      p->pa_src = src_a;
+    } else {
+      Operand o = p->op_a;
+      o.src = src_a;
+      const int32_t rc = encode_operand(o, src_a, p->dtype, p->bk, &ta, &is3d);
+      if (rc != B2G_OK) return rc;
+      if (is3d != p->kp.a_3d) return fail(B2G_ERR_INVALID_ARG, "rebind_layout_changed: create a new plan");
+    }
+  }
+  if (src_b != old_b) {
+    if (p->pack_b) {
+      p->pb_src = src_b;
+    } else {
+      Operand o = p->op_b;
+      o.src = src_b;
+      const int32_t rc = encode_operand(o, src_b, p->dtype, p->bk, &tb, &is3d);
+      if (rc != B2G_OK) return rc;
+      if (is3d != p->kp.b_3d) return fail(B2G_ERR_INVALID_ARG, "rebind_layout_changed: create a new plan");
+    }
+  }
+  p->tma_a = ta;
+  p->tma_b = tb;
+  if (p->reduce) p->r_c = C;
+  else p->kp.out = C;
+  p->user_a = A;
+  p->user_b = B;
+  p->user_c = C;
   return B2G_OK;
 }
 

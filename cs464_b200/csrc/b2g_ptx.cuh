@@ -47,6 +47,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// The same test, suspending the thread for at most about `hint_ns` while the phase is incomplete (without a hint the
+// hardware may hold the thread for its own, much longer, limit): the slow path of a bounded wait.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // ---------------------------------------------------------------- TMA
 // 2-D tiled bulk tensor load global -> shared, completion counted in bytes on `bar`.
 // x is the innermost (contiguous) coordinate; callers keep x * 2 bytes a multiple of 16.

@@ -10,6 +10,10 @@ Under autograd the forward runs the selected kernel and the backward the origina
 
 MAX_DIM is 65536: the kernels take any dimension below 2^31, and BASELINE.json config 4 needs N = 28672, above the
 reference's 16384.
+
+A routed call costs one plan lookup and one launch: plans are cached per thread and re-pointed at each call's buffers
+(`cs464_b200.matmul.gemm`). It does not read the kernels' device status word (that would be a host sync per call):
+`check_status()` raises if a bounded device wait ran out since the last check — call it at a sync point.
 """
 from __future__ import annotations
 
@@ -20,7 +24,7 @@ import warnings
 import torch
 
 from cs464_b200.keys import parse_key
-from cs464_b200.matmul import gemm
+from cs464_b200.matmul import check_status, gemm  # noqa: F401 (check_status is part of this module's API)
 
 MAX_DIM = 65536
 SAVING_FRAC_UNLOCKED = 0.04

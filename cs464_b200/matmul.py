@@ -17,7 +17,9 @@ There is no Triton, no CPU path and no other backend here: the kernels are the h
 from __future__ import annotations
 
 import ctypes
+import threading
 import weakref
+from collections import OrderedDict
 from dataclasses import asdict, dataclass, fields
 
 import torch
@@ -200,10 +202,11 @@ def matmul(a: torch.Tensor, b: torch.Tensor, cfg: MatmulConfig) -> torch.Tensor:
 
 _ABI_CFG: dict = {}
 _STATUS: dict = {}
+PLAN_CACHE_SIZE = 64  # plans kept per thread (each holds its tensor maps and, for split-K / staging, a workspace)
 
 
 def status_word(device: torch.device) -> torch.Tensor:
-    """A per-device int32 status word shared by one-shot launches (`gemm`)."""
+    """A per-device int32 status word shared by one-shot launches (`gemm`); read it with `check_status`."""
     key = device.index if device.index is not None else torch.cuda.current_device()
     t = _STATUS.get(key)
     if t is None:
@@ -211,24 +214,78 @@ def status_word(device: torch.device) -> torch.Tensor:
     return t
 
 
+def check_status(device: torch.device | int | None = None) -> None:
+    """Raise if a one-shot launch (`gemm`, the torch.matmul dispatcher) on `device` (default: every device used so
+    far) gave up a bounded device wait since the last check, and clear the word. Synchronises with the device. A
+    routed call returns without reading it (that would cost a host sync per call): call this at a sync point."""
+    devs = list(_STATUS) if device is None else [torch.device("cuda", device).index if isinstance(device, int)
+                                                 else (device.index if device.index is not None
+                                                       else torch.cuda.current_device())]
+    for d in devs:
+        t = _STATUS.get(d)
+        if t is None:
+            continue
+        code = int(t.item())
+        if code:
+            t.zero_()
+            raise RuntimeError(f"b200 kernel status 0x{code:x} on cuda:{d}: {_abi.status_string(code)} "
+                               "(results of launches since the last check may be incomplete)")
+
+
+class _Plans(threading.local):
+    def __init__(self):
+        self.plans: OrderedDict = OrderedDict()
+
+
+_PLANS = _Plans()
+
+
+class _CachedPlan:
+    __slots__ = ("plan", "ws", "_fin")
+
+    def __init__(self, plan: ctypes.c_void_p, ws):
+        self.plan = plan
+        self.ws = ws
+        self._fin = weakref.finalize(self, _abi.load().b2g_plan_destroy, plan)
+
+
 def gemm(cfg: MatmulConfig, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """One-shot C = A @ B on the current stream through `b2g_gemm` (plan, launch and free in one C call): the lean path
-    for per-call dispatch, where building a runner object per call would cost more host time than small kernels
-    take. The output is fresh each call unless `out` is given."""
+    """One-shot C = A @ B on the current stream: the path of per-call dispatch. A launch plan (tensor maps, grid,
+    workspace) is kept per thread for each (config, shape, strides, dtype, device, stream, pointer alignment); a
+    call with new buffers re-points it (`b2g_plan_rebind`: re-encodes only the tensor maps whose operand moved) and
+    launches. The output is fresh each call unless `out` is given. The device status word is not read here
+    (`check_status`)."""
     M, K = a.shape
     N = b.shape[1]
     c = out if out is not None else torch.empty((M, N), device=a.device, dtype=a.dtype)
-    acfg = _ABI_CFG.get(cfg)
-    if acfg is None:
-        acfg = _ABI_CFG[cfg] = cfg.to_abi()
     lib = _abi.load()
-    pr = problem(M, N, K, a.stride(), b.stride(), c.stride(), a.dtype)
-    n = ctypes.c_size_t(0)
-    _abi.check(lib.b2g_workspace_size(ctypes.byref(acfg), ctypes.byref(pr), a.data_ptr(), b.data_ptr(),
-                                      ctypes.byref(n)), "b2g_workspace_size")
-    ws = torch.zeros(n.value, dtype=torch.uint8, device=a.device) if n.value else None
-    rc = lib.b2g_gemm(ctypes.byref(acfg), ctypes.byref(pr), a.data_ptr(), b.data_ptr(), c.data_ptr(),
-                      ws.data_ptr() if ws is not None else None, n.value, status_word(a.device).data_ptr(),
-                      torch.cuda.current_stream(a.device).cuda_stream)
-    _abi.check(rc, "b2g_gemm")
+    dev = a.device.index if a.device.index is not None else torch.cuda.current_device()
+    stream = torch.cuda.current_stream(a.device).cuda_stream
+    pa, pb, pc = a.data_ptr(), b.data_ptr(), c.data_ptr()
+    key = (cfg, M, N, K, a.stride(), b.stride(), c.stride(), a.dtype, dev, stream, pa & 15, pb & 15, pc & 15)
+    plans = _PLANS.plans
+    ent = plans.get(key)
+    if ent is not None:
+        plans.move_to_end(key)
+        rc = lib.b2g_plan_rebind(ent.plan, pa, pb, pc)
+        if rc:
+            plans.pop(key)
+            ent = None
+    if ent is None:
+        acfg = _ABI_CFG.get(cfg)
+        if acfg is None:
+            acfg = _ABI_CFG[cfg] = cfg.to_abi()
+        pr = problem(M, N, K, a.stride(), b.stride(), c.stride(), a.dtype)
+        n = ctypes.c_size_t(0)
+        _abi.check(lib.b2g_workspace_size(ctypes.byref(acfg), ctypes.byref(pr), pa, pb, ctypes.byref(n)),
+                   "b2g_workspace_size")
+        ws = torch.zeros(n.value, dtype=torch.uint8, device=a.device) if n.value else None
+        plan = ctypes.c_void_p()
+        _abi.check(lib.b2g_plan_create(ctypes.byref(acfg), ctypes.byref(pr), pa, pb, pc,
+                                       ws.data_ptr() if ws is not None else None, n.value,
+                                       status_word(a.device).data_ptr(), ctypes.byref(plan)), "b2g_plan_create")
+        ent = plans[key] = _CachedPlan(plan, ws)
+        while len(plans) > PLAN_CACHE_SIZE:
+            plans.popitem(last=False)
+    _abi.check(lib.b2g_plan_launch(ent.plan, stream), "b2g_plan_launch")
     return c

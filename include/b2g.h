@@ -125,6 +125,13 @@ int32_t b2g_plan_create(const b2g_config* cfg, const b2g_problem* prob, const vo
    synchronisation: capturable into a CUDA graph. Returns B2G_OK, B2G_ERR_INVALID_ARG when the current device is not
    the one the plan was made on (nothing is launched), or B2G_ERR_CUDA (launch error). */
 int32_t b2g_plan_launch(const b2g_plan* plan, void* stream);
+/* Point an existing plan at new A, B and C of the same shape, strides and alignment class (each pointer's address
+   modulo 16 unchanged): only the tensor maps of operands whose address changed are re-encoded, nothing is
+   allocated, and the launch geometry is kept. The per-call path of a dispatcher that sees the same shape with new
+   buffers (the reference caches one runner per call site and pointers, lscli/client.py:328-345). Returns
+   B2G_ERR_INVALID_ARG, leaving the plan as it was, when the alignment class or the tensor-map form would change:
+   then create a new plan. Not safe while another thread launches the same plan. */
+int32_t b2g_plan_rebind(b2g_plan* plan, const void* A, const void* B, void* C);
 /* number of kernels b2g_plan_launch enqueues (packing, GEMM, split-K reduce) */
 int32_t b2g_plan_num_kernels(const b2g_plan* plan);
 /* grid size (CTAs) of the plan's GEMM kernel */

@@ -15,6 +15,7 @@ from cs464_b200.config_space import HANDPICKED
 from cs464_b200.matmul import B200Matmul, MatmulConfig
 from cs464_b200.search import screen_shape, select_kernel, shape_space
 from cs464_b200.timing import Protocol, measure_us
+from cs464_b200.keys import parse_key as parse_key_
 from cs464_b200.winner_cache import WinnerCache, environment
 
 pytestmark = pytest.mark.gpu
@@ -216,3 +217,65 @@ def test_plan_refuses_to_launch_on_another_device():
             run()
     finally:
         torch.cuda.set_device(prev)
+
+
+def test_dispatch_host_overhead(tmp_path):
+    """Host time per torch.matmul call with routing on (the reference's tests/test_lscli_client.py:349-387): an
+    undispatched call (fp32, or non-contiguous fp16) costs at most 5 us more than the unpatched function, and a
+    dispatched call at most 20 us more than the family's own make_runner + call. Median of 2,000 calls, synchronising
+    every 200 so the launch queue never fills."""
+    wc = WinnerCache(tmp_path / "wc.jsonl", env=environment())
+    key = "bm128_bn128_bk64_w4_s6_g8_sk1"
+    wc.put(128, 128, 128, "fp16", k=3, choice={"key": key, "family": "b200_sm100a_v1", "us": 3.0},
+           extra={"torch_us": 40.0})
+    a32 = torch.randn(64, 64, device="cuda")
+    h = torch.randn(128, 128, device="cuda", dtype=torch.float16)
+    hn = torch.randn(64, 64, device="cuda", dtype=torch.float16).t()
+    orig = torch.matmul
+
+    def per_call(f, x, n=2000, sync_every=200):
+        ts = []
+        for i in range(n):
+            t = time.perf_counter_ns()
+            f(x, x)
+            ts.append(time.perf_counter_ns() - t)
+            if (i + 1) % sync_every == 0:
+                torch.cuda.synchronize()
+        ts.sort()
+        return ts[len(ts) // 2] / 1e3
+    base32, base_nc = per_call(orig, a32), per_call(orig, hn)
+    dispatch.enable(cache=wc)
+    try:
+        patched32, patched_nc = per_call(torch.matmul, a32), per_call(torch.matmul, hn)
+        be = B200Matmul(parse_key_(key))
+        direct = per_call(lambda x, y: be.make_runner(x, y)(), h)
+        patched_hit = per_call(torch.matmul, h)
+        assert dispatch.stats()["routed"] >= 2000
+        print(f"\n[overhead] undispatched +{patched32 - base32:.2f} us (torch {base32:.2f} us), late exit "
+              f"+{patched_nc - base_nc:.2f} us; dispatched {patched_hit:.2f} us vs make_runner+call {direct:.2f} us")
+        assert patched32 - base32 <= 5.0 and patched_nc - base_nc <= 5.0
+        assert patched_hit - direct <= 20.0
+        torch.cuda.synchronize()
+        dispatch.check_status()
+        c = torch.matmul(h, h)
+        assert gate.check_norm_relative(c, gate.reference(h, h), h, h).valid
+    finally:
+        dispatch.disable()
+
+
+def test_one_shot_plans_are_rebound_to_new_buffers():
+    """The cached one-shot path: the same shape on new buffers (and a split-K config with its workspace) gives the
+    oracle's answer every time; a pointer with another alignment class gets a plan of its own."""
+    from cs464_b200.matmul import gemm
+    for cfg in (MatmulConfig(128, 128, 64, num_stages=6), MatmulConfig(128, 128, 64, num_stages=4, SPLIT_K=4)):
+        for seed in range(3):
+            a, b = gate.make_inputs(200, 136, 1024, seed=seed)
+            c = gemm(cfg, a, b)
+            assert gate.check_norm_relative(c, gate.reference(a, b), a, b).valid, (cfg.key(), seed)
+    buf = torch.empty(200 * 1024 + 8, device="cuda", dtype=torch.float16)
+    a, b = gate.make_inputs(200, 136, 1024, seed=7)
+    a_off = buf[8:].view(200, 1024)  # 16 bytes in: same class as a fresh tensor
+    a_off.copy_(a)
+    c = gemm(MatmulConfig(128, 128, 64, num_stages=6), a_off, b)
+    assert gate.check_norm_relative(c, gate.reference(a, b), a, b).valid
+

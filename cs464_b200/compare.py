@@ -5,11 +5,14 @@ For every shape of a suite, on one GPU, with one timing protocol (cold L2, CUDA 
             (`search.search_shape` + `choose`), then re-timed with the full protocol;
   * `best`  the family's best-in-pool over a screen of the shape-pruned space (`--space N` configs, 0 = skip);
   * `lt`    cuBLASLt's heuristic top-`lt_n`, each validated and timed: `lt0` = rank 0 (B2), `lt_best` = best (B3);
+            with `--lt-deep-s S`, also the fastest configs of a budgeted search of cuBLASLt's configuration space
+            (`cublaslt_deep`, S seconds per shape in a child process): `lt_best` is then B3+;
   * `torch` torch.matmul (B1).
 The row's `gap_sel_vs_lt` = sel / lt_best - 1 and `gap_sel_vs_best` = sel / best - 1 (the reference's regret,
 results/README.md:79); the summary gives their median and p95.
 
-    python -m cs464_b200.compare --suite config3 [--limit N] [--k 3] [--space 0] [--lt-n 16] [--out rows.jsonl]
+    python -m cs464_b200.compare --suite config3 [--limit N] [--k 3] [--space 0] [--lt-n 16] [--lt-deep-s 5]
+                                 [--out rows.jsonl]
 """
 from __future__ import annotations
 
@@ -36,7 +39,8 @@ def _time(backend, a, b) -> float:
     return measure_us(backend.make_runner(a, b), FULL, keep_samples=False).trimmed_us
 
 
-def compare_shape(shape: dict, *, k: int = 3, space: int = 0, lt_n: int = 16, ranker=None) -> dict:
+def compare_shape(shape: dict, *, k: int = 3, space: int = 0, lt_n: int = 16, ranker=None, lt_deep_s: float = 0.0,
+                  deep_cache: str = "lt_deep_cache") -> dict:
     M, N, K = shape["M"], shape["N"], shape["K"]
     dtype = torch.float16
     a, b = make_inputs(M, N, K, dtype, scale_b=shape.get("weight_std", 1.0))
@@ -69,6 +73,13 @@ def compare_shape(shape: dict, *, k: int = 3, space: int = 0, lt_n: int = 16, ra
     for c in cublaslt.candidates(M, N, K, dtype, lt_n):
         if validate(c, M, N, K, dtype, ref=ref, inputs=(a, b), norm_rel=True).valid:
             lts.append((c.rank, _time(c, a, b)))
+    if lt_deep_s > 0:
+        from cs464_b200 import cublaslt_deep
+        res = cublaslt_deep.search_isolated(M, N, K, deep_cache, budget_s=lt_deep_s)
+        row["lt_deep"] = {x: res.get(x) for x in ("n_timed", "n_seeds", "exhausted", "error")}
+        for c in cublaslt_deep.backends(res, dtype):
+            if validate(c, M, N, K, dtype, ref=ref, inputs=(a, b), norm_rel=True).valid:
+                lts.append((100 + c.rank, _time(c, a, b)))
     if lts:
         row["lt0_us"] = dict(lts).get(0)
         row["lt_best_us"] = min(t for _, t in lts)
@@ -109,19 +120,22 @@ def main(argv=None) -> dict:
     ap.add_argument("--k", type=int, default=3)
     ap.add_argument("--space", type=int, default=0)
     ap.add_argument("--lt-n", type=int, default=16)
+    ap.add_argument("--lt-deep-s", type=float, default=0.0, help="cuBLASLt configuration search budget per shape")
+    ap.add_argument("--deep-cache", default="lt_deep_cache")
     ap.add_argument("--out", default=None)
     a = ap.parse_args(argv)
     shapes = suites.load(a.suite)[: a.limit]
     rows = []
     for s in shapes:
-        r = compare_shape(s, k=a.k, space=a.space, lt_n=a.lt_n)
+        r = compare_shape(s, k=a.k, space=a.space, lt_n=a.lt_n, lt_deep_s=a.lt_deep_s, deep_cache=a.deep_cache)
         rows.append(r)
         print(json.dumps(r), flush=True)
         if a.out:
             with open(a.out, "a") as f:
                 f.write(json.dumps(r) + "\n")
     summary = summarize(rows)
-    print(json.dumps({"summary": summary, "suite": a.suite, "k": a.k, "space": a.space}), flush=True)
+    print(json.dumps({"summary": summary, "suite": a.suite, "k": a.k, "space": a.space, "lt_n": a.lt_n,
+                      "lt_deep_s": a.lt_deep_s}), flush=True)
     return summary
 
 

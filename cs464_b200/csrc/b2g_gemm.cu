@@ -352,9 +352,13 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     gemm_kernel(const __grid_constant__ KParams p, const __grid_constant__ CUtensorMap tma_a,
                 const __grid_constant__ CUtensorMap tma_b) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // Let a programmatically dependent launch (the split-K reduce) be scheduled once every CTA of this grid is
-  // running; the dependent waits for this grid's completion before it reads anything.
+  // Let a programmatically dependent launch (the split-K reduce, or the next GEMM) be scheduled once every CTA of this
+  // grid is running; the dependent waits for this grid's completion before it touches global memory.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // This grid may itself be such a dependent: its set-up (barriers, tensor memory, descriptor prefetch) overlaps the
+  // previous kernel's tail, and every thread waits for that kernel to complete (its writes visible) before its first
+  // global access — A and B may be its outputs, and C or the workspace its inputs. Without the launch attribute the
+  // wait returns at once.
   const uint32_t ctl = smem_addr(smem_raw);
   const uint32_t data = (ctl + kCtlBytes + 1023u) & ~1023u;
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem_raw + OFF_ABORT);
@@ -455,7 +459,10 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     // barriers so far, and the other roles wait on them after the barrier below. One stage, not the whole ring:
     // issuing more delays the barrier, and with it the first MMA. A pair's copies signal the leader's barriers,
     // which exist only after the cluster barrier.
-    if (!PAIR) produce(1, ctl + OFF_FULL);
+    if (!PAIR) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      produce(1, ctl + OFF_FULL);
+    }
   }
   if (warp == 1) {
     if (PAIR) {
@@ -476,6 +483,7 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     __syncthreads();
   }
   tc_fence_after();
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(smem_raw + OFF_TMEM);
 
   if (warp == 0) {
@@ -1600,27 +1608,33 @@ int32_t b2g_plan_launch(const b2g_plan* p, void* stream) {
         p->pb_outer, p->pb_inner);
   }
   if (!p->k_zero) {
+    // a programmatic dependent of whatever precedes it on the stream: its prologue overlaps that kernel's tail
+    // (the kernel waits for it before touching global memory)
+    cudaLaunchConfig_t lc = {};
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.blockDim = dim3(p->threads, 1, 1);
+    lc.dynamicSmemBytes = p->smem;
+    lc.stream = st;
+    lc.attrs = attr;
+    cudaError_t le;
     if (p->pair) {
-      cudaLaunchConfig_t lc = {};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = 2;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
+      attr[1].id = cudaLaunchAttributeClusterDimension;
+      attr[1].val.clusterDim.x = 2;
+      attr[1].val.clusterDim.y = 1;
+      attr[1].val.clusterDim.z = 1;
       lc.gridDim = dim3(2 * p->grid, 1, 1);
-      lc.blockDim = dim3(p->threads, 1, 1);
-      lc.dynamicSmemBytes = p->smem;
-      lc.stream = st;
-      lc.attrs = attr;
-      lc.numAttrs = 1;
-      cudaError_t le = (p->epi_warps == 4) ? cudaLaunchKernelEx(&lc, gemm_kernel<4, 1>, p->kp, p->tma_a, p->tma_b)
-                                           : cudaLaunchKernelEx(&lc, gemm_kernel<8, 1>, p->kp, p->tma_a, p->tma_b);
-      if (le != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("cluster launch: ") + cudaGetErrorString(le));
-    } else if (p->epi_warps == 4) {
-      gemm_kernel<4, 0><<<p->grid, p->threads, p->smem, st>>>(p->kp, p->tma_a, p->tma_b);
+      lc.numAttrs = 2;
+      le = (p->epi_warps == 4) ? cudaLaunchKernelEx(&lc, gemm_kernel<4, 1>, p->kp, p->tma_a, p->tma_b)
+                               : cudaLaunchKernelEx(&lc, gemm_kernel<8, 1>, p->kp, p->tma_a, p->tma_b);
     } else {
-      gemm_kernel<8, 0><<<p->grid, p->threads, p->smem, st>>>(p->kp, p->tma_a, p->tma_b);
+      lc.gridDim = dim3(p->grid, 1, 1);
+      lc.numAttrs = 1;
+      le = (p->epi_warps == 4) ? cudaLaunchKernelEx(&lc, gemm_kernel<4, 0>, p->kp, p->tma_a, p->tma_b)
+                               : cudaLaunchKernelEx(&lc, gemm_kernel<8, 0>, p->kp, p->tma_a, p->tma_b);
     }
+    if (le != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("GEMM launch: ") + cudaGetErrorString(le));
   }
   if (p->reduce) {
     const int64_t work = p->r_vec ? p->r_M * p->r_N / 4 : p->r_M * p->r_N;

@@ -8,6 +8,7 @@
     gate+up (4096 -> 28672), down (14336 -> 4096), tokens M in {1, 16, 128, 2048, 8192}; weights N(0, 0.02^2).
   * config 5 `fresh_suite(seed=2)`: 1000 fresh shapes from config 3's sampler with seed 2 (config 2 is a fixed
     7-point list, so "its distribution" is read as config 3's sampler).
+  * `edge_suite`: the correctness-only edge shapes (degenerate, prime, K below one K step).
 """
 from __future__ import annotations
 
@@ -51,7 +52,23 @@ def fresh_suite(n: int = 1000, seed: int = 2) -> list[dict]:
     return random_suite(n, seed, name="fresh")
 
 
-SUITES = {"config2": square_sweep, "config3": random_suite, "config4": llama_suite, "config5": fresh_suite}
+def edge_suite() -> list[dict]:
+    """Correctness-only shapes at the kernels' edges, the dimensions of the reference's edge suite
+    (suites/generate.py:120-131): every (M, N, K) of M in {1, 17, 64, 129, 257}, N in {1, 15, 64, 127, 257},
+    K in {1, 3, 16, 33, 255, 1031} (degenerate, prime and off-by-one sizes, K below one K step); cubes of the sizes
+    around powers of two from 1 to 257; and four extremes (a 1 x 1 dot product of length 16384, a GEMV, a one-column
+    output with a prime K, and K = 8)."""
+    shapes = [{"M": m, "N": n, "K": k, "suite": "edge"}
+              for m in (1, 17, 64, 129, 257) for n in (1, 15, 64, 127, 257) for k in (1, 3, 16, 33, 255, 1031)]
+    shapes += [{"M": d, "N": d, "K": d, "suite": "edge"}
+               for d in (1, 2, 3, 7, 15, 16, 17, 31, 33, 63, 65, 127, 129, 255, 257)]
+    shapes += [{"M": m, "N": n, "K": k, "suite": "edge"}
+               for m, n, k in ((1, 1, 16384), (1, 4096, 4096), (4093, 1, 4093), (2048, 2048, 8))]
+    return shapes
+
+
+SUITES = {"config2": square_sweep, "config3": random_suite, "config4": llama_suite, "config5": fresh_suite,
+          "edge": edge_suite}
 
 
 def load(name: str) -> list[dict]:

@@ -68,10 +68,14 @@ def test_workspace_size():
     assert workspace_bytes(MatmulConfig(128, 128, 64), 512, 512, 512) == 0
     def r256(x):
         return -(-x // 256) * 256
-    # fp32 partials [4, 100, 70], then B staged: N = 70 is not a multiple of 8, so rows of 72 elements, K = 1000 rows
+    # fp32 partials [4, 100, 70], one split counter per output tile (1 x 1 tiles here), then B staged: N = 70 is not
+    # a multiple of 8, so rows of 72 elements, K = 1000 rows
     assert workspace_bytes(MatmulConfig(128, 128, 64, SPLIT_K=4), 100, 70, 1000) == r256(4 * 100 * 70 * 4) + r256(
-        1000 * 72 * 2)
-    assert workspace_bytes(MatmulConfig(128, 128, 64, SPLIT_K=4), 128, 64, 1024) == r256(4 * 128 * 64 * 4)
+        1 * 4) + r256(1000 * 72 * 2)
+    assert workspace_bytes(MatmulConfig(128, 128, 64, SPLIT_K=4), 128, 64, 1024) == r256(4 * 128 * 64 * 4) + r256(4)
+    # a CTA pair counts per half tile: 2 x 3 tiles of 256 x 256, two counters each
+    assert workspace_bytes(MatmulConfig(256, 256, 64, num_stages=6, SPLIT_K=2, CLUSTER=2), 512, 768, 1024) == r256(
+        2 * 512 * 768 * 4) + r256(2 * 3 * 2 * 4)
     lib = _abi.load()
     n = ctypes.c_size_t()
     pr = _abi.Problem(M=17, N=33, K=65, stride_am=65, stride_ak=1, stride_bk=33, stride_bn=1, stride_cm=33,

@@ -357,60 +357,58 @@ __device__ __forceinline__ void stage_flush(uint32_t stg, int lane, uint8_t* bas
 
 // Split-K, reduced in the GEMM kernel: the CTA that finished a tile's last split sums the fp32 partials of all splits
 // (in split order, so results do not depend on which split finished last, and match the separate reduce kernel bit for
-// bit) for the rows of lane quarter `q` in each 128-row half it owns and the 32-column chunks c = grp, grp + groups,
+// bit) for the rows of lane quarter `q` in each 128-row half it owns and the 16-column chunks c = grp, grp + groups,
 // ..., then writes C.
-__device__ __noinline__ void reduce_split_tile(const KParams& p, int tm, int tn, int row_base, int halves, int q,
-                                               int lane, int grp, int groups) {
+__device__ __forceinline__ void reduce_split_tile(const KParams& p, int tm, int tn, int row_base, int halves, int q,
+                                                  int lane, int grp, int groups) {
   const float* ws = static_cast<const float*>(p.out);
-  const int nchunks = (p.tile_n + 31) / 32;
+  const int nchunks = (p.tile_n + 15) / 16;  // 16 columns at a time keeps the register footprint small
   for (int h = 0; h < halves; ++h) {
     const int64_t row0 = static_cast<int64_t>(tm) * p.tile_m + row_base + h * 128 + q * 32;
     if (row0 >= p.rows_a) break;
     const int64_t row = row0 + lane;
-    const bool row_ok = row < p.rows_a;
+    if (row >= p.rows_a) continue;  // no collective operations below: lanes past the edge just skip
     for (int c = grp; c < nchunks; c += groups) {
-      const int64_t col0 = static_cast<int64_t>(tn) * p.tile_n + c * 32;
+      const int64_t col0 = static_cast<int64_t>(tn) * p.tile_n + c * 16;
       if (col0 >= p.rows_b) break;
-      const int ncol = p.rows_b - col0 < 32 ? static_cast<int>(p.rows_b - col0) : 32;
-      float acc[32];
+      const int ncol = p.rows_b - col0 < 16 ? static_cast<int>(p.rows_b - col0) : 16;
+      float acc[16];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) acc[j] = 0.f;
-      if (row_ok) {
-        for (int sp = 0; sp < p.split_k; ++sp) {
-          const float* src = ws + static_cast<int64_t>(sp) * p.out_split_stride + row * p.out_si;
-          if (p.vec_ok && ncol == 32) {
-            const float4* s4 = reinterpret_cast<const float4*>(src + col0);
+      for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+      for (int sp = 0; sp < p.split_k; ++sp) {
+        const float* src = ws + static_cast<int64_t>(sp) * p.out_split_stride + row * p.out_si;
+        if (p.vec_ok && ncol == 16) {
+          const float4* s4 = reinterpret_cast<const float4*>(src + col0);
 #pragma unroll
-            for (int k4 = 0; k4 < 8; ++k4) {
-              const float4 x = s4[k4];
-              acc[4 * k4] += x.x;
-              acc[4 * k4 + 1] += x.y;
-              acc[4 * k4 + 2] += x.z;
-              acc[4 * k4 + 3] += x.w;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < ncol) acc[j] += src[(col0 + j) * p.out_sj];
-          }
-        }
-        uint16_t* dst = static_cast<uint16_t*>(p.c_out) + row * p.c_si;
-        if (p.c_vec && ncol == 32) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + col0);
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint4 v;
-            v.x = cvt_pair(acc[8 * q4], acc[8 * q4 + 1], p.c_bf16);
-            v.y = cvt_pair(acc[8 * q4 + 2], acc[8 * q4 + 3], p.c_bf16);
-            v.z = cvt_pair(acc[8 * q4 + 4], acc[8 * q4 + 5], p.c_bf16);
-            v.w = cvt_pair(acc[8 * q4 + 6], acc[8 * q4 + 7], p.c_bf16);
-            d4[q4] = v;
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const float4 x = s4[k4];
+            acc[4 * k4] += x.x;
+            acc[4 * k4 + 1] += x.y;
+            acc[4 * k4 + 2] += x.z;
+            acc[4 * k4 + 3] += x.w;
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j < ncol) dst[(col0 + j) * p.c_sj] = cvt_one(acc[j], p.c_bf16);
+          for (int j = 0; j < 16; ++j)
+            if (j < ncol) acc[j] += src[(col0 + j) * p.out_sj];
         }
+      }
+      uint16_t* dst = static_cast<uint16_t*>(p.c_out) + row * p.c_si;
+      if (p.c_vec && ncol == 16) {
+        uint4* d4 = reinterpret_cast<uint4*>(dst + col0);
+#pragma unroll
+        for (int q4 = 0; q4 < 2; ++q4) {
+          uint4 v;
+          v.x = cvt_pair(acc[8 * q4], acc[8 * q4 + 1], p.c_bf16);
+          v.y = cvt_pair(acc[8 * q4 + 2], acc[8 * q4 + 3], p.c_bf16);
+          v.z = cvt_pair(acc[8 * q4 + 4], acc[8 * q4 + 5], p.c_bf16);
+          v.w = cvt_pair(acc[8 * q4 + 6], acc[8 * q4 + 7], p.c_bf16);
+          d4[q4] = v;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (j < ncol) dst[(col0 + j) * p.c_sj] = cvt_one(acc[j], p.c_bf16);
       }
     }
   }
@@ -418,7 +416,7 @@ __device__ __noinline__ void reduce_split_tile(const KParams& p, int tm, int tn,
 
 // One CTA (PAIR = 0) or one CTA of a pair (PAIR = 1, cluster of 2, cta_group::2 MMAs of M = 256).
 template <int EPI_WARPS, int PAIR>
-__global__ void __maxnreg__(EPI_WARPS == 8 ? 200 : 255)
+__global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     gemm_kernel(const __grid_constant__ KParams p, const __grid_constant__ CUtensorMap tma_a,
                 const __grid_constant__ CUtensorMap tma_b) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1750,7 +1748,10 @@ int32_t b2g_plan_launch(const b2g_plan* p, void* stream) {
       le = (p->epi_warps == 4) ? cudaLaunchKernelEx(&lc, gemm_kernel<4, 0>, p->kp, p->tma_a, p->tma_b)
                                : cudaLaunchKernelEx(&lc, gemm_kernel<8, 0>, p->kp, p->tma_a, p->tma_b);
     }
-    if (le != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("GEMM launch: ") + cudaGetErrorString(le));
+    if (le != cudaSuccess) {
+      cudaGetLastError();  // a refused launch is not sticky: clear it so the next call does not report it again
+      return fail(B2G_ERR_CUDA, std::string("GEMM launch: ") + cudaGetErrorString(le));
+    }
   }
   if (p->reduce) {
     const int64_t work = p->r_vec ? p->r_M * p->r_N / 4 : p->r_M * p->r_N;
@@ -1766,7 +1767,10 @@ int32_t b2g_plan_launch(const b2g_plan* p, void* stream) {
     lc.numAttrs = 1;
     cudaError_t le = cudaLaunchKernelEx(&lc, splitk_reduce_kernel, p->r_ws, p->r_c, p->r_M, p->r_N, p->r_scm,
                                         p->r_scn, p->r_split, p->r_bf16, p->r_vec);
-    if (le != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("reduce launch: ") + cudaGetErrorString(le));
+    if (le != cudaSuccess) {
+      cudaGetLastError();
+      return fail(B2G_ERR_CUDA, std::string("reduce launch: ") + cudaGetErrorString(le));
+    }
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(B2G_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));

@@ -241,7 +241,7 @@ _PLANS = _Plans()
 
 
 class _CachedPlan:
-    __slots__ = ("plan", "ws", "_fin")
+    __slots__ = ("plan", "ws", "_fin", "__weakref__")
 
     def __init__(self, plan: ctypes.c_void_p, ws):
         self.plan = plan

@@ -3,11 +3,12 @@
 
 Workload: M = N = K in {256, 512, 1024, 2048, 4096, 8192, 16384}, row-major A[M,K] and B[K,N] with i.i.d. N(0,1)
 entries cast to fp16 (CUDA generator, seed 0), fp32 accumulate, fp16 output. One step = one GEMM of every size, each
-preceded by an L2 flush (a 1 GiB write, outside the GEMM's timed interval). `value` = sum of 2*n^3 over the sizes, all
-steps and all ranks, divided by the summed device time of the GEMMs (CUDA events on the launching stream, max over
-ranks). Each size runs the config the library's first-use selection picks before the timed steps: the shipped
-ranker's top 3 plus the zero-search rule's config (cs464_b200.select), each validated and short-timed on the size's
-inputs (cs464_b200.search.measure / choose), the fastest kept; `--config KEY` forces one config instead.
+preceded by an L2 flush (a write of twice the L2 size, outside the GEMM's timed interval). `value` = sum of 2*n^3
+over the sizes, all steps and all ranks, divided by the summed device time of the GEMMs (CUDA events on the
+launching stream, max over ranks). Each size runs the config the library's first-use selection picks before the
+timed steps: the shipped ranker's top 3 plus the zero-search rule's config (cs464_b200.select), each validated and
+short-timed on the size's inputs (cs464_b200.search.measure / choose), the fastest kept; `--config KEY` forces one
+config instead.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
@@ -46,7 +47,7 @@ SEARCH_SPACE = 96
 METRIC = "fp16 GEMM TFLOP/s (% of B200 dense peak)"
 UNIT = "TFLOP/s"
 FALLBACK_PEAK_TFLOPS = 1590.0
-FLUSH_BYTES = 1 << 30
+FLUSH_L2_MULTIPLE = 2    # the L2 flush before each GEMM writes twice the device's L2 size (252 MB on B200)
 # DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of that exact launch
 # (profiles/gemm_16384_256x256x64_full.md): {(size, config key): bytes}. Other selections report null.
 TRAFFIC_BYTES = {(16384, "bm256_bn256_bk64_w4_s3_g8_sk1"): 6.761165e9 + 0.528053e9}
@@ -224,7 +225,8 @@ def search_leg(args, rank: int, world: int, dev, barrier, max_over_ranks) -> dic
 def workload_config(args) -> dict:
     return {"workload": "square_sweep_fp16 (BASELINE.json configs[1])", "sizes": args.sizes_list or SIZES,
             "inputs": "N(0,1) cast to fp16, seed 0", "layout": "row-major NN, fp32 accumulate, fp16 out",
-            "l2": "flushed before every GEMM (1 GiB write outside the timed interval)", "parallelism": "replicas"}
+            "l2": "flushed before every GEMM (a write of 2x the L2 size outside the timed interval)",
+            "parallelism": "replicas"}
 
 
 def main():
@@ -282,12 +284,15 @@ def main():
         c = torch.empty((n, n), device=dev, dtype=torch.float16)
         run = B200Matmul(cfg).make_runner(a, b, out=c)
         work.append({"n": n, "a": a, "b": b, "c": c, "cfg": cfg, "run": run, "flops": 2.0 * n ** 3})
-    flush_buf = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    flush_bytes = FLUSH_L2_MULTIPLE * torch.cuda.get_device_properties(dev).L2_cache_size
+    flush_buf = torch.empty(flush_bytes // 4, dtype=torch.int32, device=dev)
+    flush_val = [0]
     stream = torch.cuda.current_stream(dev)
 
     def one_step(record: list | None):
         for i, w in enumerate(work):
-            flush_buf.zero_()
+            flush_val[0] = (flush_val[0] + 1) & 0x7FFFFFFF
+            flush_buf.fill_(flush_val[0])  # a new value each time: every line of the buffer is rewritten
             if record is None:
                 w["run"]()
             else:

@@ -45,6 +45,7 @@ constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s per wait: far above a
 constexpr uint64_t kDrainTimeoutNs = 50000000ull;   // 50 ms to drain in-flight work after an abort
 constexpr size_t kMaxSmemPerCta = 232448;          // sm_100 opt-in maximum dynamic shared memory per block
 constexpr int kDefaultSmCount = 148;                // B200, when no device is current (host-only sizing)
+constexpr size_t kFusedReduceMaxBytes = 128u << 10;  // split-K partials one CTA sums in the GEMM kernel (per tile)
 
 // control block layout (byte offsets)
 constexpr uint32_t OFF_FULL = 0;      // kMaxStages x u64
@@ -1072,6 +1073,7 @@ struct Geometry {
   Operand a, b;  // MMA "A" (rows over tile_m) and MMA "B" (rows over tile_n)
   size_t ws_partial;  // split-K partial bytes
   size_t ws_counters;  // split-K in the GEMM kernel: per-tile (and pair-half) counters of finished splits
+  bool fused;          // split-K summed in the GEMM kernel
   int streamk;
   int64_t sk_iters;     // tiles * num_kb
   int64_t sk_max_ctas;  // upper bound on resident CTAs (sizes the fix-up slots)
@@ -1085,7 +1087,8 @@ uint32_t pow2_at_least(uint32_t x) {
   return p;
 }
 
-// `fused`: split-K partials are summed in the GEMM kernel (counters in the workspace) rather than by a second kernel.
+// `fused`: split-K partials may be summed in the GEMM kernel (counters in the workspace) rather than by a second
+// kernel; `g.fused` says whether this problem does (small per-tile partials only, see kFusedReduceMaxBytes).
 int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g, const void* A, const void* B,
                       bool fused = true) {
   if (!cfg || !pr) return fail(B2G_ERR_INVALID_ARG, "null config or problem");
@@ -1178,7 +1181,11 @@ int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g,
   if (cfg->split_k > 1 && ws_elems >= (int64_t(1) << 40))
     return fail(B2G_ERR_UNSUPPORTED, "split_k_workspace_too_large");
   g.ws_partial = cfg->split_k > 1 ? static_cast<size_t>(round_up(ws_elems * 4, 256)) : 0;
-  g.ws_counters = (cfg->split_k > 1 && fused)
+  // The CTA that finishes a tile last reads every split's partial of its cta_m x tile_n block alone; beyond
+  // kFusedReduceMaxBytes of partials that serial read costs more than a second kernel spread over all SMs.
+  g.fused = fused && cfg->split_k > 1 &&
+            static_cast<int64_t>(cfg->split_k) * g.cta_m * g.tile_n * 4 <= static_cast<int64_t>(kFusedReduceMaxBytes);
+  g.ws_counters = g.fused
                       ? static_cast<size_t>(round_up(static_cast<int64_t>(g.tiles_m) * g.tiles_n * (g.pair ? 2 : 1) * 4,
                                                      256))
                       : 0;
@@ -1454,7 +1461,7 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
     k.sk_iters = g.sk_iters;
     k.sk_flags = g.streamk ? reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + g.sk_flags_off) : nullptr;
     k.sk_slots = g.streamk ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + g.sk_slots_off) : nullptr;
-    if (cfg->split_k > 1 && fused) {
+    if (g.fused) {
       k.out = workspace;
       k.out_kind = OUT_F32_PARTIAL;
       k.out_split_stride = M * N;

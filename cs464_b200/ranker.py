@@ -305,10 +305,10 @@ class LearnedRanker(AnalyticRanker):
 
         from cs464_b200.keys import parse_key
         by_shape: dict[tuple, list[dict]] = {}
-        for r in rows:
-            by_shape.setdefault((r["M"], r["N"], r["K"]), []).append(r)
+        for r in rows:  # timings are compared within a shape (and within the unit / GPU they were taken on)
+            by_shape.setdefault((r["M"], r["N"], r["K"], r.get("group")), []).append(r)
         Xs, ys = [], []
-        for (M, N, K), rs in by_shape.items():
+        for (M, N, K, _), rs in by_shape.items():
             best = min(r["us"] for r in rs)
             Xs.append(_Pool([parse_key(r["key"]) for r in rs]).features(M, N, K))
             ys.append(np.log(np.array([r["us"] for r in rs]) / best))
@@ -358,28 +358,39 @@ def default_ranker():
 
 
 def rows_from_search(paths) -> list[dict]:
-    """Training rows {M, N, K, key, us} from sharded-search outputs (search_rank*.jsonl with screen rows)."""
+    """Training rows {M, N, K, key, us, group} from sharded-search outputs: the per-shape unit files
+    (<out>/units/<i>.jsonl, screen entries [key, us, status]) or older per-rank files (entries [key, us]); a directory
+    stands for its units/*.jsonl. `group` names the unit a timing came from: each unit ran on one GPU, so timings are
+    normalised within their unit."""
     from cs464_b200.keys import parse_key
+    files = []
+    for p in map(Path, paths):
+        files += sorted((p / "units").glob("*.jsonl")) if p.is_dir() else [p]
     out = []
-    for p in paths:
-        for line in Path(p).read_text().splitlines():
+    for f in files:
+        for line in f.read_text().splitlines():
             if not line.strip():
                 continue
-            r = json.loads(line)
-            for key, us in r.get("screen", []):
+            try:
+                r = json.loads(line)
+            except ValueError:
+                continue
+            group = f"{f}:{r.get('i', '')}:{r.get('slice', 0)}:{r.get('run', '')}"
+            for entry in r.get("screen", []):
+                key, us = entry[0], entry[1]
                 try:
                     parse_key(key)
                 except ValueError:
                     continue
                 if us and us > 0:
-                    out.append({"M": r["M"], "N": r["N"], "K": r["K"], "key": key, "us": float(us)})
+                    out.append({"M": r["M"], "N": r["N"], "K": r["K"], "key": key, "us": float(us), "group": group})
     return out
 
 
 def _main(argv=None) -> None:
     import argparse
     ap = argparse.ArgumentParser(description="train the learned ranker from sharded-search screens")
-    ap.add_argument("rows", nargs="+", help="search_rank*.jsonl files")
+    ap.add_argument("rows", nargs="+", help="sharded-search output directories (or unit / rank JSONL files)")
     ap.add_argument("--out", default=str(MODEL_STEM))
     ap.add_argument("--max-iter", type=int, default=600)
     a = ap.parse_args(argv)

@@ -3,14 +3,18 @@
 
 Workload: M = N = K in {256, 512, 1024, 2048, 4096, 8192, 16384}, row-major A[M,K] and B[K,N] with i.i.d. N(0,1)
 entries cast to fp16 (CUDA generator, seed 0), fp32 accumulate, fp16 output. One step = one GEMM of every size, each
-preceded by an L2 flush (a write of twice the L2 size, outside the GEMM's timed interval). `value` = sum of 2*n^3
-over the sizes, all steps and all ranks, divided by the summed device time of the GEMMs (CUDA events on the
-launching stream, max over ranks). Each size runs the config the library's first-use selection picks before the
-timed steps: the shipped ranker's top 3 plus the zero-search rule's config (cs464_b200.select), each validated and
-short-timed on the size's inputs (cs464_b200.search.measure / choose), the fastest kept; `--config KEY` forces one
-config instead.
+preceded by an L2 flush (a write of twice the L2 size, outside the GEMM's timed interval). By default the K steps'
+GEMMs run grouped by size, as BASELINE configs[1] times each shape (W warm-up launches, then the K timed ones), so a
+size's time does not carry the power-cap clock drop that the previous size's long GEMMs leave behind; `--order step`
+interleaves the sizes instead. `value` = sum of 2*n^3 over the sizes, all steps and all ranks, divided by the summed
+device time of the GEMMs (CUDA events on the launching stream, max over ranks). Each size runs the config the
+library's first-use selection picks before the timed steps: the shipped ranker's top 3 plus the zero-search rule's
+config (cs464_b200.select), each validated and short-timed on the size's inputs (cs464_b200.search.measure /
+choose), the fastest kept; `--config KEY` forces one config instead. On one GPU, `per_size` also carries the north
+star's comparators timed the same way on the same inputs: torch.matmul (cuBLAS, B1) and cuBLASLt best-of-search (the
+heuristic's top 8 plus the fastest of a short search of its configuration space, B3+).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--order size|step]
 
 With N > 1 (torchrun, one process per GPU) every rank runs the whole sweep on its own GPU: a GEMM does not shard,
 so the ranks are replicas ("scaling": "weak"); the process group only carries the barrier and the max-reduction
@@ -48,6 +52,9 @@ METRIC = "fp16 GEMM TFLOP/s (% of B200 dense peak)"
 UNIT = "TFLOP/s"
 FALLBACK_PEAK_TFLOPS = 1590.0
 FLUSH_L2_MULTIPLE = 2    # the L2 flush before each GEMM writes twice the device's L2 size (252 MB on B200)
+LT_TOP = 8               # cuBLASLt heuristic candidates timed per size (B3)
+LT_DEEP_S = 2.0          # default seconds of cuBLASLt configuration search per size (B3+)
+LT_DEEP_TOP = 4          # fastest configs of that search timed with the bench protocol
 # DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of that exact launch
 # (profiles/gemm_16384_256x256x64_full.md): {(size, config key): bytes}. Other selections report null.
 TRAFFIC_BYTES = {(16384, "bm256_bn256_bk64_w4_s3_g8_sk1"): 6.761165e9 + 0.528053e9}
@@ -57,13 +64,21 @@ def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--sizes", type=str, default=None, help="comma-separated square sizes (default: the full sweep)")
     ap.add_argument("--config", type=str, default=None, help="force one config key for every size")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-search", action="store_true")
+    ap.add_argument("--order", choices=("size", "step"), default="size",
+                    help="size: each size timed on its own, W warm-up then K timed launches (BASELINE configs[1]'s "
+                         "protocol); step: every timed step runs the whole sweep once, sizes interleaved")
+    ap.add_argument("--compare", choices=("none", "lt"), default="lt",
+                    help="lt: per size, torch.matmul (B1) and cuBLASLt (B3, or B3+ with --lt-deep-s) on the same "
+                         "inputs and protocol (1-GPU runs)")
+    ap.add_argument("--lt-deep-s", type=float, default=LT_DEEP_S,
+                    help="seconds of cuBLASLt configuration search per size for B3+ (0: heuristic top-N only, B3)")
     ap.add_argument("--search-shapes", type=int, default=SEARCH_SHAPES,
                     help="first N shapes of BASELINE config 5 for the sharded-search leg")
     ap.add_argument("--search-space", type=int, default=SEARCH_SPACE,
@@ -225,10 +240,175 @@ def search_leg(args, rank: int, world: int, dev, barrier, max_over_ranks) -> dic
             "timing": "host wall time between barriers, max over ranks"}
 
 
+class L2Flush:
+    """Rewrites a buffer of FLUSH_L2_MULTIPLE x the device's L2 size with a new value on every call, so no line of
+    the GEMM's operands or of the previous launch's output is left in L2."""
+
+    def __init__(self, dev):
+        import torch
+        nbytes = FLUSH_L2_MULTIPLE * torch.cuda.get_device_properties(dev).L2_cache_size
+        self.buf = torch.empty(nbytes // 4, dtype=torch.int32, device=dev)
+        self.val = 0
+
+    def __call__(self):
+        self.val = (self.val + 1) & 0x7FFFFFFF
+        self.buf.fill_(self.val)
+
+
+def time_launches(fn, steps: int, warmup: int, flush, stream) -> list[float]:
+    """Device milliseconds of `steps` launches of `fn` after `warmup` untimed ones, each launch preceded by an L2
+    flush outside its CUDA-event interval (events on the launching stream)."""
+    import torch
+    for _ in range(warmup):
+        flush()
+        fn()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for s, e in ev:
+        flush()
+        s.record(stream)
+        fn()
+        e.record(stream)
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in ev]
+
+
+def time_interleaved(fns, steps: int, warmup: int, flush, stream) -> list[list[float]]:
+    """Like time_launches for several launches at once, interleaved: one step runs every fn once, in order."""
+    import torch
+    for _ in range(warmup):
+        for fn in fns:
+            flush()
+            fn()
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in fns]
+          for _ in range(steps)]
+    for k in range(steps):
+        for fn, (s, e) in zip(fns, ev[k]):
+            flush()
+            s.record(stream)
+            fn()
+            e.record(stream)
+    torch.cuda.synchronize()
+    return [[ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(steps)] for i in range(len(fns))]
+
+
+def compare_leg(args, work, flush, stream) -> dict:
+    """Per size, the north star's comparators timed with the family's protocol on the same inputs: B1 = torch.matmul
+    (cuBLAS's default heuristic), B3 = the best of cuBLASLt's heuristic top `LT_TOP`, and (`--lt-deep-s` > 0) B3+ =
+    the best of B3 and the fastest configs of a budgeted search of cuBLASLt's configuration space
+    (cs464_b200.cublaslt_deep, in a child process). Each comparator's output is checked against the family's before
+    it is timed (the same gate the search uses); one that fails is left out."""
+    import torch
+
+    from cs464_b200 import cublaslt
+    from cs464_b200.baselines import TorchMatmul
+    from cs464_b200.gate import reference, validate
+    out = {}
+    deep_dir = tempfile.mkdtemp(prefix="b2g_ltdeep_")
+    for w in work:
+        n, a, b = w["n"], w["a"], w["b"]
+        steps = max(3, min(args.steps, 10))
+
+        def best_of(backends):
+            best = None
+            for be in backends:
+                try:
+                    r = be.make_runner(a, b)
+                    r()
+                    torch.cuda.synchronize()
+                    ms = time_launches(r, steps, 3, flush, stream)
+                except RuntimeError:
+                    continue
+                t = sum(ms) / len(ms)
+                if best is None or t < best[0]:
+                    best = (t, getattr(be, "key", "default"))
+            return best
+
+        ref = reference(a, b)
+        row = {}
+        b1 = best_of([TorchMatmul()])
+        lt = [c for c in cublaslt.candidates(n, n, n, torch.float16, LT_TOP)
+              if validate(c, n, n, n, torch.float16, ref=ref, inputs=(a, b)).valid]
+        if args.lt_deep_s > 0:
+            from cs464_b200 import cublaslt_deep
+            res = cublaslt_deep.search_isolated(n, n, n, deep_dir, budget_s=args.lt_deep_s)
+            lt += [c for c in cublaslt_deep.backends(res)[:LT_DEEP_TOP]
+                   if validate(c, n, n, n, torch.float16, ref=ref, inputs=(a, b)).valid]
+        b3 = best_of(lt)
+        for name, r in (("cublas", b1), ("cublaslt_b3plus" if args.lt_deep_s > 0 else "cublaslt_b3", b3)):
+            if r is not None:
+                row[f"{name}_tflops"] = round(w["flops"] / (r[0] / 1e3) / 1e12, 2)
+                if name != "cublas":
+                    row[f"{name}_key"] = r[1]
+        out[n] = row
+        del ref
+    return out
+
+
+def e2e_leg(args, work, dev, stream, barrier, max_over_ranks, flops_step: float, world: int) -> dict:
+    """The sweep end to end through the public API (`cs464_b200.matmul`): every step copies each size's inputs from
+    pinned host memory, multiplies, and copies the result back to pinned host memory. Copies in, GEMMs and copies out
+    run on three streams, so one size's copy back overlaps the next size's copy in and GEMM (a user pipelines the
+    same way); the caching allocator's record_stream keeps each buffer alive until every stream using it is done.
+    Timed on the device from the first copy in to the last copy out."""
+    import torch
+
+    from cs464_b200.matmul import matmul
+    host = []
+    for w in work:
+        ha = torch.empty_like(w["a"], device="cpu").pin_memory()
+        hb = torch.empty_like(w["b"], device="cpu").pin_memory()
+        hc = torch.empty_like(w["c"], device="cpu").pin_memory()
+        ha.copy_(w["a"])
+        hb.copy_(w["b"])
+        host.append((ha, hb, hc))
+    h2d = sum(ha.numel() * 2 + hb.numel() * 2 for ha, hb, _ in host)
+    d2h = sum(hc.numel() * 2 for _, _, hc in host)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def e2e_step():
+        for w, (ha, hb, hc) in zip(work, host):
+            s_in.wait_stream(stream)  # inputs may be allocated on memory the previous step's GEMM just released
+            with torch.cuda.stream(s_in):
+                a = ha.to(dev, non_blocking=True)
+                b = hb.to(dev, non_blocking=True)
+            stream.wait_stream(s_in)
+            a.record_stream(stream)
+            b.record_stream(stream)
+            c = matmul(a, b, w["cfg"])
+            s_out.wait_stream(stream)
+            with torch.cuda.stream(s_out):
+                hc.copy_(c, non_blocking=True)
+            c.record_stream(s_out)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(args.steps, 5))
+    s.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    stream.wait_stream(s_out)
+    e.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    for (_, _, hc), w in zip(host, work):
+        if not torch.equal(hc, w["c"].cpu()):
+            raise RuntimeError(f"end-to-end result differs from the device-timed result at {w['n']}^3")
+    e2e_ms = max_over_ranks(s.elapsed_time(e))
+    return {"value": round(flops_step * e2e_steps * world / (e2e_ms / 1e3) / 1e12, 3), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 3),
+            "api": "cs464_b200.matmul(a, b, cfg) on tensors copied from pinned host memory, result copied back; "
+                   "copies in, GEMMs and copies out on three streams"}
+
+
 def workload_config(args) -> dict:
     return {"workload": "square_sweep_fp16 (BASELINE.json configs[1])", "sizes": args.sizes_list or SIZES,
             "inputs": "N(0,1) cast to fp16, seed 0", "layout": "row-major NN, fp32 accumulate, fp16 out",
             "l2": "flushed before every GEMM (a write of 2x the L2 size outside the timed interval)",
+            "order": ("per size: W warm-up then K timed launches" if getattr(args, "order", "size") == "size"
+                      else "interleaved: every step runs each size once"),
             "parallelism": "replicas"}
 
 
@@ -244,7 +424,7 @@ def main():
     import torch.distributed as dist
 
     from cs464_b200.keys import parse_key
-    from cs464_b200.matmul import B200Matmul, matmul
+    from cs464_b200.matmul import B200Matmul
     from cs464_b200.gate import reference
     from cs464_b200.ranker import default_ranker
     from cs464_b200.search import FAMILY, choose, measure
@@ -287,40 +467,23 @@ def main():
         c = torch.empty((n, n), device=dev, dtype=torch.float16)
         run = B200Matmul(cfg).make_runner(a, b, out=c)
         work.append({"n": n, "a": a, "b": b, "c": c, "cfg": cfg, "run": run, "flops": 2.0 * n ** 3})
-    flush_bytes = FLUSH_L2_MULTIPLE * torch.cuda.get_device_properties(dev).L2_cache_size
-    flush_buf = torch.empty(flush_bytes // 4, dtype=torch.int32, device=dev)
-    flush_val = [0]
+    flush = L2Flush(dev)
     stream = torch.cuda.current_stream(dev)
 
-    def one_step(record: list | None):
-        for i, w in enumerate(work):
-            flush_val[0] = (flush_val[0] + 1) & 0x7FFFFFFF
-            flush_buf.fill_(flush_val[0])  # a new value each time: every line of the buffer is rewritten
-            if record is None:
-                w["run"]()
-            else:
-                s, e = record[i]
-                s.record(stream)
-                w["run"]()
-                e.record(stream)
-
-    for _ in range(args.warmup):
-        one_step(None)
-    torch.cuda.synchronize()
     uuid = str(torch.cuda.get_device_properties(dev).uuid)
     sampler = ClockSampler(uuid)
-    events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in work]
-              for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize()
     sampler.start()
-    for k in range(args.steps):
-        one_step(events[k])
+    if args.order == "size":
+        # BASELINE configs[1]'s protocol: each size timed on its own (warm-up launches, then the timed ones)
+        per_launch_ms = [time_launches(w["run"], args.steps, args.warmup, flush, stream) for w in work]
+    else:
+        per_launch_ms = time_interleaved([w["run"] for w in work], args.steps, args.warmup, flush, stream)
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()
-    per_size_ms = [sum(events[k][i][0].elapsed_time(events[k][i][1]) for k in range(args.steps)) / args.steps
-                   for i in range(len(work))]
+    per_size_ms = [sum(x) / len(x) for x in per_launch_ms]
     total_ms = sum(per_size_ms) * args.steps
     total_ms_max = max_over_ranks(total_ms)
     flops_step = sum(w["flops"] for w in work)
@@ -334,44 +497,13 @@ def main():
     achieved = work[dom]["flops"] / (per_size_ms[dom] / 1e3) / 1e12
     traffic = TRAFFIC_BYTES.get((work[dom]["n"], work[dom]["cfg"].key()))
 
-    # end to end through the public API: pinned host inputs copied in, matmul(), result copied back, every step
-    e2e = None
-    if not args.no_e2e:
-        host = []
-        for w in work:
-            ha = torch.empty_like(w["a"], device="cpu").pin_memory()
-            hb = torch.empty_like(w["b"], device="cpu").pin_memory()
-            hc = torch.empty_like(w["c"], device="cpu").pin_memory()
-            ha.copy_(w["a"])
-            hb.copy_(w["b"])
-            host.append((ha, hb, hc))
-        h2d = sum(ha.numel() * 2 + hb.numel() * 2 for ha, hb, _ in host)
-        d2h = sum(hc.numel() * 2 for _, _, hc in host)
+    # the comparators of the north star on the same inputs and protocol (rank 0 of a 1-GPU run: the driver's
+    # per-size reference line), timed after the family so they do not change its thermal history
+    compare = None
+    if rank == 0 and world == 1 and args.compare != "none":
+        compare = compare_leg(args, work, flush, stream)
 
-        def e2e_step():
-            for w, (ha, hb, hc) in zip(work, host):
-                a = ha.to(dev, non_blocking=True)
-                b = hb.to(dev, non_blocking=True)
-                c = matmul(a, b, w["cfg"])
-                hc.copy_(c, non_blocking=True)
-
-        for _ in range(args.warmup):
-            e2e_step()
-        torch.cuda.synchronize()
-        barrier()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e2e_steps = max(1, min(args.steps, 5))
-        s.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
-        e.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        e2e_ms = max_over_ranks(s.elapsed_time(e))
-        e2e = {"value": round(flops_step * e2e_steps * world / (e2e_ms / 1e3) / 1e12, 3), "unit": UNIT,
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "ms_per_step": round(e2e_ms / e2e_steps, 3),
-               "api": "cs464_b200.matmul(a, b, cfg) on tensors copied from pinned host memory, result copied back"}
+    e2e = None if args.no_e2e else e2e_leg(args, work, dev, stream, barrier, max_over_ranks, flops_step, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -394,7 +526,8 @@ def main():
         "config": {**workload_config(args), "selection": {str(w["n"]): w["cfg"].key() for w in work}},
         "pct_of_peak": round(100.0 * value / world / peak, 2),
         "per_size": {str(w["n"]): {"tflops": round(w["flops"] / (per_size_ms[i] / 1e3) / 1e12, 2),
-                                   "ms": round(per_size_ms[i], 4)} for i, w in enumerate(work)},
+                                   "ms": round(per_size_ms[i], 4), **((compare or {}).get(w["n"], {}))}
+                     for i, w in enumerate(work)},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": f"b2g::gemm_kernel at {work[dom]['n']}^3 ({work[dom]['cfg'].key()})",

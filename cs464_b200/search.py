@@ -4,7 +4,8 @@ Mirrors the reference's callers of its GEMM family:
   * `candidates_for(spec, M, N, K)`: backend spec strings -> `Candidate`s (tune/runner.py:42-142); specs here:
     `b200:handpicked`, `b200:heuristic`, `b200:rank[:k]`, `b200:space[:n]`, `b200:<config key>`, `torch` (B1).
   * `measure`: validate, then short-time each candidate on one placement; a burst-amortised pass when the fastest
-    cold time is under 50 us; optional reverse-order confirmation (tune/online.py:244-329).
+    cold time is under 50 us, a sustained pass (under the power cap's settled clock) when the fastest is 1 ms or
+    more; optional reverse-order confirmation (tune/online.py:244-329).
   * `choose` (tune/online.py:125-138), `search_shape` (:332-363), `select_kernel` with the winner cache and the
     call-count k policy (:58-77, :379-483).
   * `screen_shape`: times every statically and shape-pruned config with the reference's stage-1 rule (one cold sample;
@@ -23,7 +24,7 @@ from cs464_b200.config_space import HANDPICKED, HwLimits, full_space, prune, sha
 from cs464_b200.gate import ContextPoisoned, context_poisoned, make_inputs, reference, validate
 from cs464_b200.keys import parse_key
 from cs464_b200.matmul import B200Matmul, MatmulConfig
-from cs464_b200.timing import SHORT_BURST, SHORT_COLD, SMALL_US, Protocol, measure_us
+from cs464_b200.timing import LONG_US, SHORT_BURST, SHORT_COLD, SMALL_US, Protocol, measure_us, sustained
 
 FAMILY = B200Matmul.family
 DTYPE_NAMES = {torch.float16: "fp16", torch.bfloat16: "bf16"}
@@ -169,13 +170,19 @@ def measure(M: int, N: int, K: int, dtype, backends: list[tuple], *, inputs=None
             x["burst_us"] = measure_us(bk[x["config_key"]].make_runner(a, b), SHORT_BURST,
                                        keep_samples=False).median_us
             x["time_s"] += time.perf_counter() - t
+    elif ok and min(x["cold_us"] for x in ok) >= LONG_US:
+        for x in ok:
+            t = time.perf_counter()
+            x["sustained_us"] = measure_us(bk[x["config_key"]].make_runner(a, b), sustained(x["cold_us"]),
+                                           keep_samples=False).median_us
+            x["time_s"] += time.perf_counter() - t
     if confirm > 0 and ok:
-        small = all("burst_us" in x for x in ok)
-        metric = "burst_us" if small else "cold_us"
+        metric = _metric(ok)
+        proto = {"burst_us": lambda x: SHORT_BURST, "cold_us": lambda x: SHORT_COLD,
+                 "sustained_us": lambda x: sustained(x["cold_us"])}[metric]
         for x in reversed(sorted(ok, key=lambda x: x[metric])[:confirm]):
             t = time.perf_counter()
-            again = measure_us(bk[x["config_key"]].make_runner(a, b), SHORT_BURST if small else SHORT_COLD,
-                               keep_samples=False).median_us
+            again = measure_us(bk[x["config_key"]].make_runner(a, b), proto(x), keep_samples=False).median_us
             x["confirm_us"] = 0.5 * (x[metric] + again)
             x["time_s"] += time.perf_counter() - t
         for x in ok:
@@ -183,19 +190,28 @@ def measure(M: int, N: int, K: int, dtype, backends: list[tuple], *, inputs=None
     return {"candidates": cands}
 
 
+def _metric(ok: list[dict]) -> str:
+    """The time a set of valid candidates is compared by: burst time when every one has it (the fastest cold time
+    was under SMALL_US), sustained time when every one has it (the fastest was LONG_US or more), else cold time."""
+    if all(x.get("burst_us") is not None for x in ok) and min(x["cold_us"] for x in ok) < SMALL_US:
+        return "burst_us"
+    if all(x.get("sustained_us") is not None for x in ok):
+        return "sustained_us"
+    return "cold_us"
+
+
 def choose(cands: list[dict], k: int | None = None) -> dict:
-    """Fastest valid candidate among the first k (all for None): by burst time when every valid candidate has one
-    (the fastest cold time was under 50 us), else by cold time; `confirm_us` overrides when present."""
+    """Fastest valid candidate among the first k (all for None), by `_metric`'s time; `confirm_us` overrides when
+    present."""
     c = cands if k is None else cands[:k]
     ok = [x for x in c if x["valid"] and x.get("cold_us") is not None]
     cost = {"setup_s": sum(x.get("setup_s", 0.0) for x in c), "time_s": sum(x.get("time_s", 0.0) for x in c)}
     if not ok:
         return {"key": None, "mode": None, **cost}
-    small = all(x.get("burst_us") is not None for x in ok) and min(x["cold_us"] for x in ok) < SMALL_US
-    metric = "burst_us" if small else "cold_us"
+    metric = _metric(ok)
     best = min(ok, key=lambda x: x.get("confirm_us", x[metric]))
     return {"key": best["config_key"], "family": best.get("family", FAMILY), "rank": c.index(best),
-            "mode": "burst" if small else "cold", "us": best.get("confirm_us", best[metric]), **cost}
+            "mode": metric[:-3], "us": best.get("confirm_us", best[metric]), **cost}
 
 
 def search_shape(ranker, M: int, N: int, K: int, k: int, dtype=torch.float16, order: str = "diverse",

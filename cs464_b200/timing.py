@@ -18,7 +18,10 @@ How a measurement runs (`measure_us(fn, protocol)`):
 `fn` must only enqueue work on the current stream of the timed device and allocate nothing (B200Matmul runners and
 `torch.matmul(..., out=)` qualify). The short protocols of the online search: `SHORT_COLD` (10 cold samples) and,
 for kernels under `SMALL_US`, `SHORT_BURST` (5 samples of 20 back-to-back launches) — the reference's
-tune/online.py:47-55 counts.
+tune/online.py:47-55 counts. Kernels of `LONG_US` or more are also timed by `sustained(us)`: back-to-back launches
+for `SUSTAIN_S` first, so the samples see the clock the 1000 W power cap settles at. A B200 keeps its top clock for
+a few milliseconds of dense tensor work only; among long GEMMs the fastest in a short cold sample (per clock) and the
+fastest under a sustained load (per joule) can differ.
 """
 from __future__ import annotations
 
@@ -58,6 +61,17 @@ class Protocol:
 
 SHORT_COLD = Protocol(mode="cold", samples=10, max_samples=10, warmup=1, ci_target=math.inf, max_s=1.0)
 SHORT_BURST = Protocol(mode="hot", samples=5, max_samples=5, warmup=1, burst=20, ci_target=math.inf, max_s=1.0)
+LONG_US = 1000.0
+SUSTAIN_S = 0.3
+
+
+def sustained(us: float) -> Protocol:
+    """Protocol for a kernel of about `us` microseconds (>= LONG_US): SUSTAIN_S of untimed back-to-back launches, then
+    5 samples of about 20 ms of back-to-back launches each (a kernel this long fills L2 and more by itself, so no
+    flush is needed between launches)."""
+    us = max(us, 1.0)
+    return Protocol(mode="hot", samples=5, max_samples=5, warmup=max(1, int(SUSTAIN_S * 1e6 / us)),
+                    burst=max(1, int(round(20_000.0 / us))), ci_target=math.inf, max_s=10.0)
 
 
 @dataclass

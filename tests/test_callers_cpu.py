@@ -240,6 +240,12 @@ def test_choose_and_policy():
     small = [{"config_key": "a", "valid": True, "cold_us": 20.0, "burst_us": 9.0},
              {"config_key": "b", "valid": True, "cold_us": 19.0, "burst_us": 10.0}]
     assert choose(small)["key"] == "a" and choose(small)["mode"] == "burst"
+    # long kernels: the per-clock winner of the cold samples loses under the power cap's settled clock
+    long = [{"config_key": "pair", "valid": True, "cold_us": 6500.0, "sustained_us": 8100.0},
+            {"config_key": "single", "valid": True, "cold_us": 6800.0, "sustained_us": 6900.0}]
+    assert choose(long)["key"] == "single" and choose(long)["mode"] == "sustained"
+    assert timing.sustained(6500.0).warmup * 6500.0 >= 0.9 * timing.SUSTAIN_S * 1e6
+    assert timing.sustained(6500.0).mode == "hot" and timing.sustained(100.0).burst == 200
     assert choose([{"config_key": "x", "valid": False}])["key"] is None
     assert KPolicy().k_for() == 3 and KPolicy().k_for(calls=2_000_000) == 5 and KPolicy().k_for(frequent=True) == 5
 

@@ -416,10 +416,15 @@ __device__ __forceinline__ void reduce_split_tile(const KParams& p, int tm, int 
 }
 
 // One CTA (PAIR = 0) or one CTA of a pair (PAIR = 1, cluster of 2, cta_group::2 MMAs of M = 256).
-template <int EPI_WARPS, int PAIR>
+// LEAN = 1 (single CTAs only): the launch has one CTA per work unit (no stream-K, split-K reduced by the separate
+// kernel), so the unit walk, the stream-K fix-up and the in-kernel split-K sum are compiled out. A small GEMM's time is
+// mostly fixed cost, and much of that is fetching the instructions its warps execute from a cold cache: the lean form
+// executes far fewer of them.
+template <int EPI_WARPS, int PAIR, int LEAN = 0>
 __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     gemm_kernel(const __grid_constant__ KParams p, const __grid_constant__ CUtensorMap tma_a,
                 const __grid_constant__ CUtensorMap tma_b) {
+  static_assert(!(LEAN && PAIR), "the lean form is single-CTA only");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // Let a programmatically dependent launch (the split-K reduce, or the next GEMM) be scheduled once every CTA of this
   // grid is running; the dependent waits for this grid's completion before it touches global memory.
@@ -438,6 +443,17 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
   const bool leader = rank == 0;
   const int first_unit = PAIR ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
   const int unit_step = PAIR ? static_cast<int>(num_clusters_x()) : static_cast<int>(gridDim.x);
+  // every role walks the same sequence of units; the lean form has exactly one, this CTA's
+  auto next_unit = [&](Cursor& c, Unit& w) -> bool {
+    if constexpr (LEAN) {
+      if (c.u < 0) return false;
+      w = decode_unit(p, c.u);
+      c.u = -1;
+      return true;
+    } else {
+      return cursor_next(p, c, unit_step, w);
+    }
+  };
 
   // ---------------------------------------------------------------- TMA producer state (thread 0)
   // The producer walks (unit, K block) pairs in order; `produce(n)` issues copies until n stages are in flight in
@@ -453,7 +469,7 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     while (pok && pissued < max_issue) {
       while (pkb >= pkb1) {  // next unit with at least one K block
         Unit w;
-        if (!cursor_next(p, pc, unit_step, w)) return;
+        if (!next_unit(pc, w)) return;
         pkb = w.kb0;
         pkb1 = w.kb1;
         prow_a = w.tm * p.tile_m + static_cast<int>(rank) * p.cta_m;
@@ -609,7 +625,7 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
       Cursor mc;
       cursor_init(p, mc, first_unit, unit_step);
       Unit w;
-      while (ok && cursor_next(p, mc, unit_step, w)) {
+      while (ok && next_unit(mc, w)) {
         if (w.kb0 == w.kb1) continue;
         if (!mbar_try_wait(ctl + OFF_TEMPTY + 8 * acc, acc_ph ^ 1u) &&
             !wait_phase(ctl + OFF_TEMPTY + 8 * acc, acc_ph ^ 1u, abort_flag, p.status, p.timeout_ns,
@@ -722,11 +738,11 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
     Cursor ec;
     cursor_init(p, ec, first_unit, unit_step);
     Unit w;
-    while (cursor_next(p, ec, unit_step, w)) {
+    while (next_unit(ec, w)) {
       const bool zero = w.kb0 == w.kb1;
       // stream-K: a segment covering only part of its tile either contributes a partial (it does not hold the
       // tile's first K block) or owns the tile and adds the contributors' partials
-      const bool partial = p.streamk && !(w.kb0 == 0 && w.kb1 == p.num_kb);
+      const bool partial = !LEAN && p.streamk && !(w.kb0 == 0 && w.kb1 == p.num_kb);
       const bool contrib = partial && w.kb0 > 0;
       const bool owner = partial && w.kb0 == 0;
       int j_end = first_unit + 1;  // contributors of an owned tile: workers first_unit + 1 .. j_end - 1
@@ -874,7 +890,7 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
           acc_ph ^= 1u;
         }
       }
-      if (p.fused_reduce) {
+      if (!LEAN && p.fused_reduce) {
         // this split's partial is stored (the accumulator is already back with the MMA warp): count it; the last
         // split of the tile (per CTA of a pair) reduces. Release: every thread's partial stores precede the count.
         __threadfence();
@@ -1243,6 +1259,8 @@ int32_t init_device(int dev, int& sm_count) {
     if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_kernel<8, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_kernel<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_kernel<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_kernel<4, 0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_kernel<8, 0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     // a pair is a 2-CTA cluster: always within the portable size, no opt-in needed
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
     d.err = e;
@@ -1310,6 +1328,7 @@ struct b2g_plan {
   CUtensorMap tma_a, tma_b;
   int epi_warps;
   int pair;
+  int lean;        // one CTA per unit, no stream-K or in-kernel split-K sum: the lean kernel form
   int grid, threads;
   size_t smem;
   // packing
@@ -1581,6 +1600,7 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
       }
     }
     p->grid = static_cast<int>(std::max<int64_t>(grid, 1));
+    p->lean = !g.pair && !g.streamk && !g.fused && grid == g.units;
   }
   p->user_a = A;
   p->user_b = B;
@@ -1752,8 +1772,12 @@ int32_t b2g_plan_launch(const b2g_plan* p, void* stream) {
     } else {
       lc.gridDim = dim3(p->grid, 1, 1);
       lc.numAttrs = 1;
-      le = (p->epi_warps == 4) ? cudaLaunchKernelEx(&lc, gemm_kernel<4, 0>, p->kp, p->tma_a, p->tma_b)
-                               : cudaLaunchKernelEx(&lc, gemm_kernel<8, 0>, p->kp, p->tma_a, p->tma_b);
+      if (p->lean)
+        le = (p->epi_warps == 4) ? cudaLaunchKernelEx(&lc, gemm_kernel<4, 0, 1>, p->kp, p->tma_a, p->tma_b)
+                                 : cudaLaunchKernelEx(&lc, gemm_kernel<8, 0, 1>, p->kp, p->tma_a, p->tma_b);
+      else
+        le = (p->epi_warps == 4) ? cudaLaunchKernelEx(&lc, gemm_kernel<4, 0>, p->kp, p->tma_a, p->tma_b)
+                                 : cudaLaunchKernelEx(&lc, gemm_kernel<8, 0>, p->kp, p->tma_a, p->tma_b);
     }
     if (le != cudaSuccess) {
       cudaGetLastError();  // a refused launch is not sticky: clear it so the next call does not report it again

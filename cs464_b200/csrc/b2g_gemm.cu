@@ -45,7 +45,6 @@ constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s per wait: far above a
 constexpr uint64_t kDrainTimeoutNs = 50000000ull;   // 50 ms to drain in-flight work after an abort
 constexpr size_t kMaxSmemPerCta = 232448;          // sm_100 opt-in maximum dynamic shared memory per block
 constexpr int kDefaultSmCount = 148;                // B200, when no device is current (host-only sizing)
-constexpr size_t kFusedReduceMaxBytes = 128u << 10;  // split-K partials one CTA sums in the GEMM kernel (per tile)
 
 // control block layout (byte offsets)
 constexpr uint32_t OFF_FULL = 0;      // kMaxStages x u64
@@ -56,7 +55,6 @@ constexpr uint32_t OFF_DRAIN = 288;   // u64: all MMAs of this CTA complete
 constexpr uint32_t OFF_TMEM = 296;    // u32: tensor-memory base address written by tcgen05.alloc
 constexpr uint32_t OFF_ABORT = 300;   // u32: set when any role gave up waiting
 constexpr uint32_t OFF_EPISYNC = 304; // u64: epilogue-warps rendezvous (stream-K fix-up), bounded like every wait
-constexpr uint32_t OFF_LAST = 312;    // u32: this CTA finished a split-K tile last and reduces it
 
 // status codes written to the caller's device status word
 constexpr int kStatusProducerTimeout = 0x101;
@@ -108,14 +106,6 @@ struct KParams {
   // whole 16-byte pieces): the staging area starts `epi_stage_off` bytes after the operand ring.
   int32_t stage_c;
   uint32_t epi_stage_off;
-  // Split-K reduced in this kernel: each CTA counts its finished partials per tile (and pair half) in
-  // `tile_counters` (zero between launches); the last split of a tile sums every split's partial in split order and
-  // writes C at `c_out` (element (i, j) of the MMA orientation at c_out + i * c_si + j * c_sj).
-  int32_t fused_reduce;
-  int* tile_counters;
-  void* c_out;
-  int64_t c_si, c_sj;
-  int32_t c_bf16, c_vec;
   int* status;
   uint64_t timeout_ns;
   // stream-K: workers (CTAs, or CTA pairs) share sk_iters = tiles * num_kb K blocks in equal contiguous slices; a tile
@@ -354,65 +344,6 @@ __device__ __forceinline__ void stage_flush(uint32_t stg, int lane, uint8_t* bas
     if (rr < rows && pp < pieces) *reinterpret_cast<uint4*>(base + rr * row_bytes + pp * 16) = x;
   }
   __syncwarp();
-}
-
-// Split-K, reduced in the GEMM kernel: the CTA that finished a tile's last split sums the fp32 partials of all splits
-// (in split order, so results do not depend on which split finished last, and match the separate reduce kernel bit for
-// bit) for the rows of lane quarter `q` in each 128-row half it owns and the 16-column chunks c = grp, grp + groups,
-// ..., then writes C.
-__device__ __forceinline__ void reduce_split_tile(const KParams& p, int tm, int tn, int row_base, int halves, int q,
-                                                  int lane, int grp, int groups) {
-  const float* ws = static_cast<const float*>(p.out);
-  const int nchunks = (p.tile_n + 15) / 16;  // 16 columns at a time keeps the register footprint small
-  for (int h = 0; h < halves; ++h) {
-    const int64_t row0 = static_cast<int64_t>(tm) * p.tile_m + row_base + h * 128 + q * 32;
-    if (row0 >= p.rows_a) break;
-    const int64_t row = row0 + lane;
-    if (row >= p.rows_a) continue;  // no collective operations below: lanes past the edge just skip
-    for (int c = grp; c < nchunks; c += groups) {
-      const int64_t col0 = static_cast<int64_t>(tn) * p.tile_n + c * 16;
-      if (col0 >= p.rows_b) break;
-      const int ncol = p.rows_b - col0 < 16 ? static_cast<int>(p.rows_b - col0) : 16;
-      float acc[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-      for (int sp = 0; sp < p.split_k; ++sp) {
-        const float* src = ws + static_cast<int64_t>(sp) * p.out_split_stride + row * p.out_si;
-        if (p.vec_ok && ncol == 16) {
-          const float4* s4 = reinterpret_cast<const float4*>(src + col0);
-#pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {
-            const float4 x = s4[k4];
-            acc[4 * k4] += x.x;
-            acc[4 * k4 + 1] += x.y;
-            acc[4 * k4 + 2] += x.z;
-            acc[4 * k4 + 3] += x.w;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (j < ncol) acc[j] += src[(col0 + j) * p.out_sj];
-        }
-      }
-      uint16_t* dst = static_cast<uint16_t*>(p.c_out) + row * p.c_si;
-      if (p.c_vec && ncol == 16) {
-        uint4* d4 = reinterpret_cast<uint4*>(dst + col0);
-#pragma unroll
-        for (int q4 = 0; q4 < 2; ++q4) {
-          uint4 v;
-          v.x = cvt_pair(acc[8 * q4], acc[8 * q4 + 1], p.c_bf16);
-          v.y = cvt_pair(acc[8 * q4 + 2], acc[8 * q4 + 3], p.c_bf16);
-          v.z = cvt_pair(acc[8 * q4 + 4], acc[8 * q4 + 5], p.c_bf16);
-          v.w = cvt_pair(acc[8 * q4 + 6], acc[8 * q4 + 7], p.c_bf16);
-          d4[q4] = v;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (j < ncol) dst[(col0 + j) * p.c_sj] = cvt_one(acc[j], p.c_bf16);
-      }
-    }
-  }
 }
 
 // One CTA (PAIR = 0) or one CTA of a pair (PAIR = 1, cluster of 2, cta_group::2 MMAs of M = 256).
@@ -890,25 +821,6 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
           acc_ph ^= 1u;
         }
       }
-      if (!LEAN && p.fused_reduce) {
-        // this split's partial is stored (the accumulator is already back with the MMA warp): count it; the last
-        // split of the tile (per CTA of a pair) reduces. Release: every thread's partial stores precede the count.
-        __threadfence();
-        volatile uint32_t* last = reinterpret_cast<volatile uint32_t*>(smem_raw + OFF_LAST);
-        if (!epilogue_sync()) break;
-        if (epi_tid == 0) {
-          int* ctr = p.tile_counters + (PAIR ? 2 * w.tile + static_cast<int>(rank) : w.tile);
-          const int before = atomicAdd(ctr, 1);
-          const bool is_last = before == p.split_k - 1;
-          if (is_last) atomicExch(ctr, 0);  // zero again for the next launch
-          *last = is_last ? 1u : 0u;
-        }
-        if (!epilogue_sync()) break;
-        if (*last) {
-          __threadfence();  // acquire: the other splits' partials, published before their counts
-          reduce_split_tile(p, w.tm, w.tn, static_cast<int>(rank) * p.cta_m, halves, q, lane, grp, kGroups);
-        }
-      }
     }
   }
 
@@ -1088,8 +1000,6 @@ struct Geometry {
   size_t smem;
   Operand a, b;  // MMA "A" (rows over tile_m) and MMA "B" (rows over tile_n)
   size_t ws_partial;  // split-K partial bytes
-  size_t ws_counters;  // split-K in the GEMM kernel: per-tile (and pair-half) counters of finished splits
-  bool fused;          // split-K summed in the GEMM kernel
   int streamk;
   int64_t sk_iters;     // tiles * num_kb
   int64_t sk_max_ctas;  // upper bound on resident CTAs (sizes the fix-up slots)
@@ -1103,10 +1013,7 @@ uint32_t pow2_at_least(uint32_t x) {
   return p;
 }
 
-// `fused`: split-K partials may be summed in the GEMM kernel (counters in the workspace) rather than by a second
-// kernel; `g.fused` says whether this problem does (small per-tile partials only, see kFusedReduceMaxBytes).
-int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g, const void* A, const void* B,
-                      bool fused = true) {
+int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g, const void* A, const void* B) {
   if (!cfg || !pr) return fail(B2G_ERR_INVALID_ARG, "null config or problem");
   if (pr->dtype != B2G_DTYPE_F16 && pr->dtype != B2G_DTYPE_BF16)
     return fail(B2G_ERR_INVALID_ARG, "dtype must be B2G_DTYPE_F16 or B2G_DTYPE_BF16");
@@ -1197,14 +1104,6 @@ int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g,
   if (cfg->split_k > 1 && ws_elems >= (int64_t(1) << 40))
     return fail(B2G_ERR_UNSUPPORTED, "split_k_workspace_too_large");
   g.ws_partial = cfg->split_k > 1 ? static_cast<size_t>(round_up(ws_elems * 4, 256)) : 0;
-  // The CTA that finishes a tile last reads every split's partial of its cta_m x tile_n block alone; beyond
-  // kFusedReduceMaxBytes of partials that serial read costs more than a second kernel spread over all SMs.
-  g.fused = fused && cfg->split_k > 1 &&
-            static_cast<int64_t>(cfg->split_k) * g.cta_m * g.tile_n * 4 <= static_cast<int64_t>(kFusedReduceMaxBytes);
-  g.ws_counters = g.fused
-                      ? static_cast<size_t>(round_up(static_cast<int64_t>(g.tiles_m) * g.tiles_n * (g.pair ? 2 : 1) * 4,
-                                                     256))
-                      : 0;
   size_t sk_bytes = 0;
   g.sk_iters = static_cast<int64_t>(g.tiles_m) * g.tiles_n * g.num_kb;
   g.sk_max_ctas = 0;
@@ -1230,14 +1129,13 @@ int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g,
   if (K == 0) {
     // An empty K only zero-fills C: no GEMM launch, so no partials, fix-up state or staged operands are needed.
     g.ws_partial = 0;
-    g.ws_counters = 0;
     sk_bytes = 0;
     g.a.pack = g.b.pack = 0;
   }
-  // workspace: [split-K partials][split-K counters][stream-K flags + slots][staged A][staged B]
-  g.sk_flags_off += g.ws_partial + g.ws_counters;
-  g.sk_slots_off += g.ws_partial + g.ws_counters;
-  g.a.ws_off = g.ws_partial + g.ws_counters + sk_bytes;
+  // workspace: [split-K partials][stream-K flags + slots][staged A][staged B]
+  g.sk_flags_off += g.ws_partial;
+  g.sk_slots_off += g.ws_partial;
+  g.a.ws_off = g.ws_partial + sk_bytes;
   g.b.ws_off = g.a.ws_off + packed_bytes(g.a);
   g.ws_total = g.b.ws_off + packed_bytes(g.b);
   return B2G_OK;
@@ -1380,12 +1278,10 @@ int grid_for(int64_t work, int per_block) {
 }
 
 // Fill `p` (caller-owned) with the launch plan of (cfg, prob) on the current device.
-// `fused`: split-K partials are summed by the GEMM kernel itself (the last split of each tile), not by a second
-// kernel; the allocation-free entry point keeps the second kernel (its scratch keeps no counters).
 int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, const void* A, const void* B, void* C,
-                  void* workspace, size_t workspace_bytes, int32_t* status, bool fused = true) {
+                  void* workspace, size_t workspace_bytes, int32_t* status) {
   Geometry g;
-  int32_t rc = make_geometry(cfg, prob, g, A, B, fused);
+  int32_t rc = make_geometry(cfg, prob, g, A, B);
   if (rc != B2G_OK) return rc;
   const int64_t M = prob->M, N = prob->N, K = prob->K;
   if ((M > 0 && N > 0) && (!C || (K > 0 && (!A || !B)))) return fail(B2G_ERR_INVALID_ARG, "null A, B or C");
@@ -1480,21 +1376,7 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
     k.sk_iters = g.sk_iters;
     k.sk_flags = g.streamk ? reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + g.sk_flags_off) : nullptr;
     k.sk_slots = g.streamk ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + g.sk_slots_off) : nullptr;
-    if (g.fused) {
-      k.out = workspace;
-      k.out_kind = OUT_F32_PARTIAL;
-      k.out_split_stride = M * N;
-      k.out_si = g.swapped ? 1 : N;
-      k.out_sj = g.swapped ? N : 1;
-      k.vec_ok = (k.out_sj == 1) && (k.out_si % 4 == 0);
-      k.fused_reduce = 1;
-      k.tile_counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + g.ws_partial);
-      k.c_out = C;
-      k.c_si = g.swapped ? prob->stride_cn : prob->stride_cm;
-      k.c_sj = g.swapped ? prob->stride_cm : prob->stride_cn;
-      k.c_bf16 = bf16;
-      k.c_vec = (k.c_sj == 1) && (k.c_si % 8 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
-    } else if (cfg->split_k > 1) {
+    if (cfg->split_k > 1) {
       k.out = workspace;
       k.out_kind = OUT_F32_PARTIAL;
       k.out_split_stride = M * N;
@@ -1600,7 +1482,7 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
       }
     }
     p->grid = static_cast<int>(std::max<int64_t>(grid, 1));
-    p->lean = !g.pair && !g.streamk && !g.fused && grid == g.units;
+    p->lean = !g.pair && !g.streamk && grid == g.units;
   }
   p->user_a = A;
   p->user_b = B;
@@ -1853,7 +1735,6 @@ int32_t b2g_plan_rebind(b2g_plan* p, const void* A, const void* B, void* C) {
   p->tma_a = ta;
   p->tma_b = tb;
   if (p->reduce) p->r_c = C;
-  else if (p->kp.fused_reduce) p->kp.c_out = C;
   else p->kp.out = C;
   p->user_a = A;
   p->user_b = B;
@@ -1902,7 +1783,7 @@ int32_t b2g_splitk_reduce(const float* ws, void* C, int64_t M, int64_t N, int64_
 int32_t b2g_gemm_noalloc(const b2g_config* cfg, const b2g_problem* prob, const void* A, const void* B, void* C,
                          int32_t* status, void* stream) {
   Geometry g;
-  int32_t rc = make_geometry(cfg, prob, g, A, B, false);
+  int32_t rc = make_geometry(cfg, prob, g, A, B);
   if (rc != B2G_OK) return rc;
   if (g.streamk)
     return fail(B2G_ERR_UNSUPPORTED,
@@ -1927,7 +1808,7 @@ int32_t b2g_gemm_noalloc(const b2g_config* cfg, const b2g_problem* prob, const v
   if (rc != B2G_OK) return rc;
   // Nothing in the scratch needs clearing: each call's GEMM writes every partial element its reduce then reads.
   b2g_plan plan;
-  rc = plan_init(&plan, cfg, prob, A, B, C, scratch, kNoAllocScratchBytes, status, false);
+  rc = plan_init(&plan, cfg, prob, A, B, C, scratch, kNoAllocScratchBytes, status);
   if (rc != B2G_OK) return rc;
   return b2g_plan_launch(&plan, stream);
 }

@@ -69,18 +69,16 @@ def test_workspace_size():
     def r256(x):
         return -(-x // 256) * 256
     # fp32 partials [4, 100, 70], then B staged: N = 70 is not a multiple of 8, so rows of 72 elements, K = 1000 rows.
-    # 4 splits x 128 x 128 fp32 per tile is more than one CTA sums in the GEMM kernel: the second kernel reduces, and
-    # the workspace holds no split counters
+    # the second kernel sums the splits: the workspace is the partials (and any staged operand), nothing else
     assert workspace_bytes(MatmulConfig(128, 128, 64, SPLIT_K=4), 100, 70, 1000) == r256(4 * 100 * 70 * 4) + r256(
         1000 * 72 * 2)
     assert workspace_bytes(MatmulConfig(128, 128, 64, SPLIT_K=4), 128, 64, 1024) == r256(4 * 128 * 64 * 4)
-    # small per-tile partials (swapped 128 x 16 tiles, 4 splits: 32 KB) are summed in the GEMM kernel: one counter
-    # per tile, 8 x 2 tiles
     assert workspace_bytes(MatmulConfig(16, 128, 128, num_stages=6, GROUP_M=1, SPLIT_K=4), 24, 1000, 2048) == r256(
-        4 * 24 * 1000 * 4) + r256(8 * 2 * 4)
-    # a CTA pair counts per half tile: 2 x 2 tiles of 256 x 128 (128 KB of partials per CTA), two counters each
+        4 * 24 * 1000 * 4)
+    assert workspace_bytes(MatmulConfig(128, 64, 64, num_stages=6, GROUP_M=1, SPLIT_K=2), 512, 256, 2048) == r256(
+        2 * 512 * 256 * 4)
     assert workspace_bytes(MatmulConfig(256, 128, 64, num_stages=6, SPLIT_K=2, CLUSTER=2), 512, 256, 1024) == r256(
-        2 * 512 * 256 * 4) + r256(2 * 2 * 2 * 4)
+        2 * 512 * 256 * 4)
     lib = _abi.load()
     n = ctypes.c_size_t()
     pr = _abi.Problem(M=17, N=33, K=65, stride_am=65, stride_ak=1, stride_bk=33, stride_bn=1, stride_cm=33,

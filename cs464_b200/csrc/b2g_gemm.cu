@@ -853,6 +853,9 @@ __global__ void pack_kernel(const uint16_t* __restrict__ src, int64_t s_outer, i
 
 // C[m, n] = cast(sum_{s < split} ws[s, m, n]) in increasing s (the reference's fixed-order reduce,
 // kernels/triton_matmul.py:85-92). vec: N % 4 == 0, scn == 1, scm % 4 == 0 and C 8-byte aligned.
+// The loads of four splits are issued before their additions (the additions keep increasing s, so the sum is the
+// same bit for bit): a thread's time is about split / 4 memory latencies, not split of them. With the few threads a
+// decode GEMM's output needs, that latency chain is the whole kernel.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ C, int64_t M, int64_t N,
                                      int64_t scm, int64_t scn, int split, int bf16, int vec) {
   // Launched as a programmatic dependent of the GEMM (its launch overlaps the GEMM's tail): wait until the GEMM
@@ -862,10 +865,25 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* __restr
   const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
   uint16_t* c = static_cast<uint16_t*>(C);
   if (vec) {
-    for (int64_t q = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; q < MN / 4; q += step) {
+    const float4* w4 = reinterpret_cast<const float4*>(ws);
+    const int64_t mn4 = MN / 4;
+    for (int64_t q = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; q < mn4; q += step) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int s = 0; s < split; ++s) {
-        const float4 x = reinterpret_cast<const float4*>(ws + s * MN)[q];
+      int s = 0;
+      for (; s + 4 <= split; s += 4) {
+        float4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = w4[(s + u) * mn4 + q];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          acc.x += x[u].x;
+          acc.y += x[u].y;
+          acc.z += x[u].z;
+          acc.w += x[u].w;
+        }
+      }
+      for (; s < split; ++s) {
+        const float4 x = w4[s * mn4 + q];
         acc.x += x.x;
         acc.y += x.y;
         acc.z += x.z;
@@ -883,7 +901,15 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* __restr
   }
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < MN; idx += step) {
     float acc = 0.f;
-    for (int s = 0; s < split; ++s) acc += ws[s * MN + idx];
+    int s = 0;
+    for (; s + 4 <= split; s += 4) {
+      float x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u] = ws[(s + u) * MN + idx];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc += x[u];
+    }
+    for (; s < split; ++s) acc += ws[s * MN + idx];
     const int64_t m = idx / N;
     const int64_t n = idx - m * N;
     c[m * scm + n * scn] = cvt_one(acc, bf16);

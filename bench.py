@@ -57,7 +57,7 @@ LT_DEEP_S = 2.0          # default seconds of cuBLASLt configuration search per 
 LT_DEEP_TOP = 4          # fastest configs of that search timed with the bench protocol
 # DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of that exact launch
 # (profiles/gemm_16384_256x256x64_full.md): {(size, config key): bytes}. Other selections report null.
-TRAFFIC_BYTES = {(16384, "bm256_bn256_bk64_w4_s3_g8_sk1"): 6.761165e9 + 0.528053e9}
+TRAFFIC_BYTES = {(16384, "bm256_bn256_bk64_w4_s3_g8_sk1"): 8.809398e9 + 0.531044e9}
 
 
 def parse_args():
@@ -475,11 +475,13 @@ def main():
     barrier()
     torch.cuda.synchronize()
     sampler.start()
+    torch.cuda.nvtx.range_push("timed")  # `ncu --nvtx --nvtx-include timed/` lists exactly these launches
     if args.order == "size":
         # BASELINE configs[1]'s protocol: each size timed on its own (warm-up launches, then the timed ones)
         per_launch_ms = [time_launches(w["run"], args.steps, args.warmup, flush, stream) for w in work]
     else:
         per_launch_ms = time_interleaved([w["run"] for w in work], args.steps, args.warmup, flush, stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()

@@ -304,6 +304,9 @@ def compare_leg(args, work, flush, stream) -> dict:
     from cs464_b200.gate import reference, validate
     out = {}
     deep_dir = tempfile.mkdtemp(prefix="b2g_ltdeep_")
+    if args.lt_deep_s > 0:  # one child process searches every size (the per-size calls below then read its results)
+        from cs464_b200 import cublaslt_deep
+        cublaslt_deep.search_batch_isolated([(w["n"],) * 3 for w in work], deep_dir, budget_s=args.lt_deep_s)
     for w in work:
         n, a, b = w["n"], w["a"], w["b"]
         steps = max(3, min(args.steps, 10))

@@ -125,6 +125,10 @@ def main(argv=None) -> dict:
     ap.add_argument("--out", default=None)
     a = ap.parse_args(argv)
     shapes = suites.load(a.suite)[: a.limit]
+    if a.lt_deep_s > 0:  # one child process searches cuBLASLt's space for every shape first (cached per shape)
+        from cs464_b200 import cublaslt_deep
+        cublaslt_deep.search_batch_isolated([(s["M"], s["N"], s["K"]) for s in shapes], a.deep_cache,
+                                            budget_s=a.lt_deep_s)
     rows = []
     for s in shapes:
         r = compare_shape(s, k=a.k, space=a.space, lt_n=a.lt_n, lt_deep_s=a.lt_deep_s, deep_cache=a.deep_cache)

@@ -16,13 +16,15 @@ until the budget runs out; the fastest `top_k` distinct configs come back as run
 top 16 (`cs464_b200.cublaslt.candidates`) is B3+.
 
 The search runs in a child process (`python -m cs464_b200.cublaslt_deep M N K --out F`), so a configuration that
-faults cannot take the caller down; its result is cached as JSON per shape and budget.
+faults cannot take the caller down; its result is cached as JSON per shape and budget. `search_batch_isolated` fills
+that cache for a whole suite from one child (`--batch shapes.json --cache-dir D`).
 """
 from __future__ import annotations
 
 import argparse
 import ctypes as C
 import json
+import os
 import random
 import subprocess
 import sys
@@ -270,14 +272,28 @@ def search(M: int, N: int, K: int, dtype=torch.float16, budget_s: float = 10.0, 
             "best_seed_us": min((t["us"] for t in timed if t["from"] == "seed"), default=None), "top": top}
 
 
+def _cache_path(cache_dir: str | Path, M: int, N: int, K: int, dtype: str, budget_s: float) -> Path:
+    return Path(cache_dir) / f"{M}x{N}x{K}_{dtype}_b{budget_s:g}.json"
+
+
+def _cached(path: Path) -> dict | None:
+    if path.exists():
+        try:
+            d = json.loads(path.read_text())
+        except ValueError:
+            return None
+        if d.get("version") == VERSION:
+            return d
+    return None
+
+
 def search_isolated(M: int, N: int, K: int, cache_dir: str | Path, *, dtype: str = "float16", budget_s: float = 10.0,
                     top_k: int = 8, timeout_s: float = 300.0) -> dict:
     """`search` in a child process on the current GPU, cached as JSON per (shape, dtype, budget)."""
-    path = Path(cache_dir) / f"{M}x{N}x{K}_{dtype}_b{budget_s:g}.json"
-    if path.exists():
-        d = json.loads(path.read_text())
-        if d.get("version") == VERSION:
-            return d
+    path = _cache_path(cache_dir, M, N, K, dtype, budget_s)
+    d = _cached(path)
+    if d is not None:
+        return d
     path.parent.mkdir(parents=True, exist_ok=True)
     cmd = [sys.executable, "-m", "cs464_b200.cublaslt_deep", str(M), str(N), str(K), "--dtype", dtype,
            "--budget-s", str(budget_s), "--top-k", str(top_k), "--device", str(torch.cuda.current_device()),
@@ -294,6 +310,32 @@ def search_isolated(M: int, N: int, K: int, cache_dir: str | Path, *, dtype: str
         path.write_text(json.dumps(d))
         return d
     return json.loads(path.read_text())
+
+
+def search_batch_isolated(shapes: list[tuple[int, int, int]], cache_dir: str | Path, *, dtype: str = "float16",
+                          budget_s: float = 10.0, top_k: int = 8) -> int:
+    """Fill `search_isolated`'s cache for many shapes from ONE child process: one interpreter and CUDA start-up
+    (several seconds) instead of one per shape. The child writes each shape's file as soon as it is done, so a child
+    that dies part-way (a configuration that faults) loses only the shapes after it; `search_isolated` then searches
+    those in a child of their own. Returns how many shapes the child was given."""
+    todo = [(M, N, K) for M, N, K in dict.fromkeys(tuple(x) for x in shapes)
+            if _cached(_cache_path(cache_dir, M, N, K, dtype, budget_s)) is None]
+    if not todo:
+        return 0
+    Path(cache_dir).mkdir(parents=True, exist_ok=True)
+    lst = Path(cache_dir) / f"batch_{os.getpid()}.json"
+    lst.write_text(json.dumps(todo))
+    cmd = [sys.executable, "-m", "cs464_b200.cublaslt_deep", "--batch", str(lst), "--cache-dir", str(cache_dir),
+           "--dtype", dtype, "--budget-s", str(budget_s), "--top-k", str(top_k), "--device",
+           str(torch.cuda.current_device())]
+    try:
+        subprocess.run(cmd, cwd=Path(__file__).resolve().parent.parent, capture_output=True, text=True,
+                       timeout=60.0 + len(todo) * (budget_s + 10.0))
+    except subprocess.TimeoutExpired:
+        pass
+    finally:
+        lst.unlink(missing_ok=True)
+    return len(todo)
 
 
 def backends(result: dict, dtype=torch.float16) -> list:
@@ -315,17 +357,30 @@ def backends(result: dict, dtype=torch.float16) -> list:
 
 
 def _main(argv=None) -> None:
-    ap = argparse.ArgumentParser(description="budgeted cuBLASLt configuration search for one shape")
-    ap.add_argument("M", type=int)
-    ap.add_argument("N", type=int)
-    ap.add_argument("K", type=int)
+    ap = argparse.ArgumentParser(description="budgeted cuBLASLt configuration search for one shape (or a batch)")
+    ap.add_argument("M", type=int, nargs="?")
+    ap.add_argument("N", type=int, nargs="?")
+    ap.add_argument("K", type=int, nargs="?")
     ap.add_argument("--dtype", default="float16")
     ap.add_argument("--budget-s", type=float, default=10.0)
     ap.add_argument("--top-k", type=int, default=8)
     ap.add_argument("--device", type=int, default=0)
-    ap.add_argument("--out", required=True)
+    ap.add_argument("--out", help="result file of the one shape")
+    ap.add_argument("--batch", help="JSON list of [M, N, K] shapes, each written to --cache-dir as it finishes")
+    ap.add_argument("--cache-dir")
     a = ap.parse_args(argv)
     torch.cuda.set_device(a.device)
+    if a.batch:
+        if not a.cache_dir:
+            ap.error("--batch needs --cache-dir")
+        for M, N, K in json.loads(Path(a.batch).read_text()):
+            path = _cache_path(a.cache_dir, M, N, K, a.dtype, a.budget_s)
+            if _cached(path) is None:
+                d = search(M, N, K, getattr(torch, a.dtype), a.budget_s, a.top_k)
+                path.write_text(json.dumps(d))
+        return
+    if a.M is None or a.N is None or a.K is None or not a.out:
+        ap.error("give M N K and --out, or --batch")
     d = search(a.M, a.N, a.K, getattr(torch, a.dtype), a.budget_s, a.top_k)
     Path(a.out).write_text(json.dumps(d))
 

@@ -161,8 +161,10 @@ __device__ __forceinline__ int64_t sk_start(const KParams& p, int64_t w) {
 }
 
 // The sequence of work items of one worker: units worker, worker + workers, ... (tiles or split-K units). With
-// stream-K: first the worker's whole tiles of the data-parallel waves, then the (tile, K range) segments of its slice
-// of the shared K blocks. Every role walks the same sequence.
+// stream-K: first the (tile, K range) segments of its slice of the shared K blocks, then its whole tiles of the
+// data-parallel waves. Shared segments first: an owner's fix-up (waiting for its contributors' partials, adding them)
+// then runs in its epilogue while its MMA warp already works on the next tile, instead of after the last one; and a
+// contributor never waits, so the owners' waits all end. Every role walks the same sequence.
 struct Cursor {
   int64_t it, hi;
   int u;
@@ -180,6 +182,16 @@ __device__ __forceinline__ void cursor_init(const KParams& p, Cursor& c, int wor
 
 __device__ __forceinline__ bool cursor_next(const KParams& p, Cursor& c, int workers, Unit& w) {
   if (p.streamk) {
+    if (c.it < c.hi) {  // a (tile, K range) segment of this worker's slice of the shared K blocks
+      const int64_t t = c.it / p.num_kb;
+      w.kb0 = static_cast<int>(c.it - t * p.num_kb);
+      w.kb1 = static_cast<int>(min(static_cast<int64_t>(p.num_kb), w.kb0 + (c.hi - c.it)));
+      w.tile = static_cast<int>(t);
+      w.split = 0;
+      tile_coords(p, w.tile, w.tm, w.tn);
+      c.it += w.kb1 - w.kb0;
+      return true;
+    }
     if (c.u < p.sk_dp_tiles) {  // a whole tile of the data-parallel waves
       w.tile = c.u;
       w.split = 0;
@@ -189,15 +201,7 @@ __device__ __forceinline__ bool cursor_next(const KParams& p, Cursor& c, int wor
       c.u += workers;
       return true;
     }
-    if (c.it >= c.hi) return false;
-    const int64_t t = c.it / p.num_kb;
-    w.kb0 = static_cast<int>(c.it - t * p.num_kb);
-    w.kb1 = static_cast<int>(min(static_cast<int64_t>(p.num_kb), w.kb0 + (c.hi - c.it)));
-    w.tile = static_cast<int>(t);
-    w.split = 0;
-    tile_coords(p, w.tile, w.tm, w.tn);
-    c.it += w.kb1 - w.kb0;
-    return true;
+    return false;
   }
   if (c.u >= p.units) return false;
   w = decode_unit(p, c.u);
@@ -640,28 +644,30 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
       return ok;
     };
     const int64_t slot_elems = static_cast<int64_t>(p.cta_m) * p.tile_n;
-    float* const my_slot = p.streamk ? p.sk_slots + static_cast<int64_t>(blockIdx.x) * slot_elems : nullptr;
+    // A stream-K slot holds a CTA's cta_m x tile_n fp32 partial as float4 pieces ordered [32-column chunk][piece of
+    // 4 columns][row]: the 32 lanes of a warp (32 consecutive rows) store or load 512 contiguous bytes per
+    // instruction. `piece0` = chunk * 8 + first piece, in pieces of cta_m float4s.
+    auto slot_piece = [&](int64_t slot, int piece, int row_local) -> int64_t {
+      return slot * (slot_elems / 4) + static_cast<int64_t>(piece) * p.cta_m + row_local;
+    };
     // Stream-K owner: add the fp32 partials that contributors j0 .. j1-1 (later K blocks, in worker order) left for
-    // `ncol` columns at offset `off` of their slots, in that fixed order.
-    auto add_partials = [&](uint32_t (&v)[32], int64_t off, int ncol, int j0, int j1) {
+    // `ncol` columns (32-column chunk `chunk`, row `row_local`) of their slots, in that fixed order.
+    auto add_partials = [&](uint32_t (&v)[32], int chunk, int row_local, int ncol, int j0, int j1) {
+      const float4* slots4 = reinterpret_cast<const float4*>(p.sk_slots);
       for (int j = j0; j < j1; ++j) {
-        const float4* src = reinterpret_cast<const float4*>(
-            p.sk_slots + static_cast<int64_t>(PAIR ? 2 * j + static_cast<int>(rank) : j) * slot_elems + off);
+        const int64_t slot = PAIR ? 2 * j + static_cast<int>(rank) : j;
+        float4 x[8];  // the chunk's eight 16-byte pieces in flight together: one memory latency per contributor
 #pragma unroll
-        for (int h4 = 0; h4 < 8; h4 += 4) {  // four 16-byte loads in flight at a time (register pressure)
-          float4 x[4];
+        for (int k4 = 0; k4 < 8; ++k4)
+          if (k4 * 4 < ncol) x[k4] = slots4[slot_piece(slot, chunk * 8 + k4, row_local)];
 #pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4)
-            if ((h4 + k4) * 4 < ncol) x[k4] = src[h4 + k4];
-#pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {
-            const int e = 4 * (h4 + k4);
-            if (e < ncol) {
-              v[e] = __float_as_uint(__uint_as_float(v[e]) + x[k4].x);
-              v[e + 1] = __float_as_uint(__uint_as_float(v[e + 1]) + x[k4].y);
-              v[e + 2] = __float_as_uint(__uint_as_float(v[e + 2]) + x[k4].z);
-              v[e + 3] = __float_as_uint(__uint_as_float(v[e + 3]) + x[k4].w);
-            }
+        for (int k4 = 0; k4 < 8; ++k4) {
+          const int e = 4 * k4;
+          if (e < ncol) {
+            v[e] = __float_as_uint(__uint_as_float(v[e]) + x[k4].x);
+            v[e + 1] = __float_as_uint(__uint_as_float(v[e + 1]) + x[k4].y);
+            v[e + 2] = __float_as_uint(__uint_as_float(v[e + 2]) + x[k4].z);
+            v[e + 3] = __float_as_uint(__uint_as_float(v[e + 3]) + x[k4].w);
           }
         }
       }
@@ -753,9 +759,7 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
                                  v);
                   tmem_ld_wait();
                 }
-                if (owner)
-                  add_partials(v, static_cast<int64_t>(row_local) * p.tile_n + c2 * 64 + hh * 32, 32, first_unit + 1,
-                               j_end);
+                if (owner) add_partials(v, 2 * c2 + hh, row_local, 32, first_unit + 1, j_end);
                 uint4 pc[4];
 #pragma unroll
                 for (int k4 = 0; k4 < 4; ++k4) {
@@ -789,18 +793,19 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
             }
             tmem_ld_wait();
           }
-          const int64_t slot_off = static_cast<int64_t>(row_local) * p.tile_n + c * 32;
           if (contrib) {
-            float4* dst = reinterpret_cast<float4*>(my_slot + slot_off);
+            float4* slots4 = reinterpret_cast<float4*>(p.sk_slots);
+            const int64_t slot = static_cast<int64_t>(blockIdx.x);
 #pragma unroll
             for (int k4 = 0; k4 < 8; ++k4) {
               if (k4 * 4 < ncol)
-                dst[k4] = make_float4(__uint_as_float(v[4 * k4]), __uint_as_float(v[4 * k4 + 1]),
-                                      __uint_as_float(v[4 * k4 + 2]), __uint_as_float(v[4 * k4 + 3]));
+                slots4[slot_piece(slot, c * 8 + k4, row_local)] =
+                    make_float4(__uint_as_float(v[4 * k4]), __uint_as_float(v[4 * k4 + 1]),
+                                __uint_as_float(v[4 * k4 + 2]), __uint_as_float(v[4 * k4 + 3]));
             }
             continue;
           }
-          if (owner) add_partials(v, slot_off, ncol, first_unit + 1, j_end);  // contributors' partials, K order
+          if (owner) add_partials(v, c, row_local, ncol, first_unit + 1, j_end);  // contributors' partials, K order
           store_chunk(p, w.split, row, static_cast<int64_t>(w.tn) * p.tile_n + c * 32, ncol, v);
         }
       }

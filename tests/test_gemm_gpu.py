@@ -137,10 +137,10 @@ def test_stream_k_deterministic_and_correct(cfg):
                          ids=lambda c: c.key())
 @pytest.mark.parametrize("shape", [(3328, 3328, 2048), (4096, 4096, 1024), (4096, 4096, 4096)])
 def test_stream_k_schedules_at_wave_edges(cfg, shape):
-    """Both stream-K policies: full data-parallel waves with the partial last wave's tiles split evenly in K
-    (3328^2: 169 tiles on 148 SMs; 4096^2 pairs: 256 tiles on 74 pairs), and the shared-K hybrid when the last wave
-    is more than half full (4096^2 single CTAs: 256 tiles on 148 SMs). Outputs through the staged epilogue, owners
-    adding their contributors' partials; bitwise stable run to run."""
+    """Both stream-K cases: full data-parallel waves with the partial last wave's tiles split evenly in K (3328^2:
+    169 tiles on 148 SMs; 4096^2 pairs: 256 tiles on 74 pairs), and plain data-parallel waves when the last wave is
+    more than half full (4096^2 single CTAs: 256 tiles on 148 SMs). Outputs through the staged epilogue, owners adding
+    their contributors' partials; bitwise stable run to run."""
     M, N, K = shape
     a, b = oracle.make_inputs(M, N, K, seed=5)
     run = B200Matmul(cfg).make_runner(a.cuda(), b.cuda())

@@ -55,9 +55,10 @@ FLUSH_L2_MULTIPLE = 2    # the L2 flush before each GEMM writes twice the device
 LT_TOP = 8               # cuBLASLt heuristic candidates timed per size (B3)
 LT_DEEP_S = 2.0          # default seconds of cuBLASLt configuration search per size (B3+)
 LT_DEEP_TOP = 4          # fastest configs of that search timed with the bench protocol
-# DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu capture of that exact launch
-# (profiles/gemm_16384_256x256x64_full.md): {(size, config key): bytes}. Other selections report null.
-TRAFFIC_BYTES = {(16384, "bm256_bn256_bk64_w4_s3_g8_sk1"): 8.809398e9 + 0.531044e9}
+# DRAM bytes (read + write) of one launch of the dominant kernel, from one single-pass ncu capture of that exact
+# launch (profiles/gemm_16384_256x256x64_full.md): {(size, config key): bytes}. Other selections report null.
+TRAFFIC_BYTES = {(16384, "bm256_bn256_bk64_w4_s3_g16_sk1"): 6.464091e9 + 0.527321e9,
+                 (16384, "bm256_bn256_bk64_w4_s3_g8_sk1"): 6.796216e9 + 0.524988e9}
 
 
 def parse_args():

@@ -348,6 +348,35 @@ def compare_leg(args, work, flush, stream) -> dict:
     return out
 
 
+def _pin_to_gpu_numa_node(dev):
+    """Run this process on the CPUs NVML lists as closest to `dev` (a property of this process only, not of the GPU),
+    so the pinned host buffers allocated next sit on that GPU's NUMA node; returns the previous CPU set to restore,
+    or None when NVML or the affinity call is unavailable."""
+    try:
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(dev).uuid).replace("GPU-", "")
+        h = None
+        for i in range(pynvml.nvmlDeviceGetCount()):  # NVML's order may differ from CUDA's: match by UUID
+            u = pynvml.nvmlDeviceGetUUID(pynvml.nvmlDeviceGetHandleByIndex(i))
+            if uuid in (u.decode() if isinstance(u, bytes) else u):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                break
+        if h is None:
+            return None
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, 64)
+        cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (int(w) >> b) & 1}
+        old = os.sched_getaffinity(0)
+        cpus &= set(range(os.cpu_count() or 1))
+        if not cpus or cpus == old:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return old
+    except Exception:
+        return None
+
+
 def e2e_leg(args, work, dev, stream, barrier, max_over_ranks, flops_step: float, world: int) -> dict:
     """The sweep end to end through the public API (`cs464_b200.matmul`): every step copies each size's inputs from
     pinned host memory, multiplies, and copies the result back to pinned host memory. Copies in, GEMMs and copies out
@@ -357,6 +386,7 @@ def e2e_leg(args, work, dev, stream, barrier, max_over_ranks, flops_step: float,
     import torch
 
     from cs464_b200.matmul import matmul
+    restore = _pin_to_gpu_numa_node(dev)  # pinned buffers on the GPU's own NUMA node (matters with 8 ranks per host)
     host = []
     for w in work:
         ha = torch.empty_like(w["a"], device="cpu").pin_memory()
@@ -401,6 +431,8 @@ def e2e_leg(args, work, dev, stream, barrier, max_over_ranks, flops_step: float,
         if not torch.equal(hc, w["c"].cpu()):
             raise RuntimeError(f"end-to-end result differs from the device-timed result at {w['n']}^3")
     e2e_ms = max_over_ranks(s.elapsed_time(e))
+    if restore is not None:
+        os.sched_setaffinity(0, restore)
     return {"value": round(flops_step * e2e_steps * world / (e2e_ms / 1e3) / 1e12, 3), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 3),
             "api": "cs464_b200.matmul(a, b, cfg) on tensors copied from pinned host memory, result copied back; "

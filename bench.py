@@ -19,7 +19,7 @@ heuristic's top 8 plus the fastest of a short search of its configuration space,
 With N > 1 (torchrun, one process per GPU) every rank runs the whole sweep on its own GPU: a GEMM does not shard,
 so the ranks are replicas ("scaling": "weak"); the process group only carries the barrier and the max-reduction
 of the timings. What does shard is the selector search: the `search` object of the line is BASELINE config 5's
-sharded search on a fixed 48-shape subset, the same shapes at every N, so its shapes_per_s across N is the search's
+sharded search on a fixed 96-shape subset, the same shapes at every N, so its shapes_per_s across N is the search's
 strong scaling.
 
 `--impl reference` times the reference's CPU path for the same metric: the fp32 `a.float() @ b.float()` of
@@ -46,7 +46,7 @@ sys.path.insert(0, str(ROOT))
 SIZES = [256, 512, 1024, 2048, 4096, 8192, 16384]
 CPU_SAMPLE_ROWS = 2048   # the CPU legs time every size on a block of at most this many rows of A (the rate is
                          # what is compared; a 16384^3 fp32 GEMM alone takes seconds on the host)
-SEARCH_SHAPES = 48       # sharded-search leg: the first 48 shapes of BASELINE config 5 at every N
+SEARCH_SHAPES = 96       # sharded-search leg: the first 96 shapes of BASELINE config 5 at every N
 SEARCH_SPACE = 96
 METRIC = "fp16 GEMM TFLOP/s (% of B200 dense peak)"
 UNIT = "TFLOP/s"

@@ -47,7 +47,8 @@ from pathlib import Path
 
 EXIT_POISONED = 3
 STALE_S = 90.0             # a heartbeat older than this marks its rank dead (a config never takes this long)
-UNIT_TARGET_S = 2.0        # estimated screening seconds per unit
+UNIT_TARGET_S = 0.5        # estimated screening seconds per unit: well under a rank's share at 8 GPUs
+POLL_S = 0.05              # how often a rank with nothing claimable looks at the queue again
 SCREEN_SAMPLES_EST = 16    # samples a config that is not cut gets (1 + the screen's 15)
 PER_CONFIG_HOST_S = 2.5e-3 # validation and launch overheads per config, measured on B200 runs of the screen
 FLUSH_S = 1.2e-4           # one L2 flush of the cold protocol
@@ -387,7 +388,7 @@ def run_rank(rank: int, queue_path: str, out_dir: str, cache_path: str | None, *
                 break
             if deadline_s is not None and time.perf_counter() - t0 > deadline_s:
                 break
-            time.sleep(0.25)
+            time.sleep(POLL_S)
             continue
         unit, shape, crashed = got
         u = unit["u"]

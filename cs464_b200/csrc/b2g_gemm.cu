@@ -45,6 +45,8 @@ constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s per wait: far above a
 constexpr uint64_t kDrainTimeoutNs = 50000000ull;   // 50 ms to drain in-flight work after an abort
 constexpr size_t kMaxSmemPerCta = 232448;          // sm_100 opt-in maximum dynamic shared memory per block
 constexpr int kDefaultSmCount = 148;                // B200, when no device is current (host-only sizing)
+constexpr int kMaxRedCluster = 8;                   // split-K summed in a cluster of at most 8 CTAs (portable size)
+constexpr int64_t kMaxRedElems = 8192;              // ... for tiles of at most 8192 fp32 partials (32 KB) per CTA
 
 // control block layout (byte offsets)
 constexpr uint32_t OFF_FULL = 0;      // kMaxStages x u64
@@ -117,6 +119,10 @@ struct KParams {
   int64_t sk_iters;     // (tiles - sk_dp_tiles) * num_kb
   float* sk_slots;
   int* sk_flags;
+  // split-K summed inside a cluster of the SPLIT_K CTAs of a tile (lean form only): each CTA leaves its fp32 partial
+  // in its own shared memory (laid out along C's contiguous direction: [j][i] when red_imajor, else [i][j], rows
+  // padded by 4 floats), then CTA r sums slice r of the tile over every CTA's partial in split order and writes C.
+  int32_t red_cluster, red_imajor;
 };
 
 struct Unit {
@@ -672,6 +678,42 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
         }
       }
     };
+    if (LEAN && p.red_cluster) {
+      // This CTA's partial (its K range of the tile) into its shared memory: the operand ring is free once every MMA
+      // has completed, which the accumulator barrier signals. The sum over the cluster follows the role branches.
+      const Unit w = decode_unit(p, first_unit);
+      const bool zero = w.kb0 == w.kb1;
+      if (zero || wait_phase(ctl + OFF_TFULL, 0u, abort_flag, p.status, p.timeout_ns, kStatusEpilogueTimeout)) {
+        if (!zero) tc_fence_after();
+        for (int h = 0; h < halves; ++h) {
+          const int i = h * 128 + q * 32 + lane;  // tile row (tensor-memory lane)
+          for (int c = grp; c < nchunks; c += kGroups) {
+            const int ncol = min(32, p.tile_n - c * 32);
+            uint32_t v[32];
+            if (zero) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0u;
+            } else {
+              const uint32_t taddr = tmem_base + h * p.tile_n + c * 32 + (static_cast<uint32_t>(q * 32) << 16);
+              if (ncol == 32) tmem_ld_32cols(taddr, v);
+              else tmem_ld_16cols(taddr, v);
+              tmem_ld_wait();
+            }
+            if (p.red_imajor) {  // [j][i]: the warp's 32 rows are 32 consecutive words of each column
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < ncol) st_shared_u32(data + ((c * 32 + j) * (p.tile_m + 4) + i) * 4u, v[j]);
+            } else {  // [i][j]: rows 4 floats apart in banks, so each quarter-warp's 16-byte stores are conflict-free
+#pragma unroll
+              for (int k4 = 0; k4 < 8; ++k4)
+                if (k4 * 4 < ncol)
+                  st_shared_v4(data + (i * (p.tile_n + 4) + c * 32 + k4 * 4) * 4u,
+                               make_uint4(v[4 * k4], v[4 * k4 + 1], v[4 * k4 + 2], v[4 * k4 + 3]));
+            }
+          }
+        }
+      }
+    } else {
     Cursor ec;
     cursor_init(p, ec, first_unit, unit_step);
     Unit w;
@@ -826,6 +868,87 @@ __global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
           acc_ph ^= 1u;
         }
       }
+    }
+    }
+  }
+
+  if constexpr (LEAN) {
+    if (p.red_cluster) {
+      // Every CTA of the cluster holds its partial: CTA r sums its share of the tile over all of them, in split order
+      // (0 + p0 + p1 + ...: the order, and so the bits, of the separate reduce kernel), converts and writes C. The
+      // second cluster barrier keeps each CTA's shared memory alive until its peers have read it. Every thread of
+      // every CTA reaches both barriers, also after a timed-out wait (then the status word holds the error).
+      __syncwarp();
+      cluster_sync();
+      if (warp >= 2) {
+        const int S = p.split_k;
+        const int r = static_cast<int>(cluster_ctarank());
+        const int rows = p.tile_m, cols = p.tile_n;
+        const int per = p.red_imajor ? rows / 8 : cols / 8;  // 8-element groups along C's contiguous direction
+        const int groups = (p.red_imajor ? cols : rows) * per;
+        const int g0 = static_cast<int>(static_cast<int64_t>(groups) * r / S);
+        const int g1 = static_cast<int>(static_cast<int64_t>(groups) * (r + 1) / S);
+        const Unit w = decode_unit(p, first_unit);
+        const int bf = p.out_kind == OUT_BF16;
+        uint16_t* out = static_cast<uint16_t*>(p.out);
+        for (int g = g0 + static_cast<int>(threadIdx.x) - 64; g < g1; g += EPI_WARPS * 32) {
+          int i0, j0;
+          uint32_t off;  // float offset of the group in every CTA's partial
+          if (p.red_imajor) {
+            j0 = g / per;
+            i0 = (g - j0 * per) * 8;
+            off = static_cast<uint32_t>(j0 * (rows + 4) + i0);
+          } else {
+            i0 = g / per;
+            j0 = (g - i0 * per) * 8;
+            off = static_cast<uint32_t>(i0 * (cols + 4) + j0);
+          }
+          const int64_t gi = static_cast<int64_t>(w.tm) * p.tile_m + i0;
+          const int64_t gj = static_cast<int64_t>(w.tn) * p.tile_n + j0;
+          if (gi >= p.rows_a || gj >= p.rows_b) continue;
+          float4 xa[8], xb[8];  // every split's 8 values in flight before the ordered additions
+#pragma unroll
+          for (int sp = 0; sp < 8; ++sp) {
+            if (sp < S) {
+              const uint32_t a = map_to_rank(data + off * 4u, static_cast<uint32_t>(sp));
+              xa[sp] = ld_cluster_v4(a);
+              xb[sp] = ld_cluster_v4(a + 16u);
+            }
+          }
+          float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int sp = 0; sp < 8; ++sp) {
+            if (sp < S) {
+              acc8[0] += xa[sp].x;
+              acc8[1] += xa[sp].y;
+              acc8[2] += xa[sp].z;
+              acc8[3] += xa[sp].w;
+              acc8[4] += xb[sp].x;
+              acc8[5] += xb[sp].y;
+              acc8[6] += xb[sp].z;
+              acc8[7] += xb[sp].w;
+            }
+          }
+          // the group runs along i (red_imajor) or j; elements past C's edge are skipped
+          const int64_t lim = p.red_imajor ? p.rows_a - gi : p.rows_b - gj;
+          const int64_t step = p.red_imajor ? p.out_si : p.out_sj;
+          uint16_t* dst = out + gi * p.out_si + gj * p.out_sj;
+          if (lim >= 8 && step == 1 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+            uint4 pk;
+            pk.x = cvt_pair(acc8[0], acc8[1], bf);
+            pk.y = cvt_pair(acc8[2], acc8[3], bf);
+            pk.z = cvt_pair(acc8[4], acc8[5], bf);
+            pk.w = cvt_pair(acc8[6], acc8[7], bf);
+            *reinterpret_cast<uint4*>(dst) = pk;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              if (e < lim) dst[e * step] = cvt_one(acc8[e], bf);
+          }
+        }
+      }
+      __syncwarp();
+      cluster_sync();
     }
   }
 
@@ -1036,6 +1159,7 @@ struct Geometry {
   int64_t sk_max_ctas;  // upper bound on resident CTAs (sizes the fix-up slots)
   size_t sk_flags_off, sk_slots_off;
   size_t ws_total;
+  int red_cluster;  // split-K summed in a cluster of the tile's CTAs through shared memory: no partials in the workspace
 };
 
 uint32_t pow2_at_least(uint32_t x) {
@@ -1044,7 +1168,58 @@ uint32_t pow2_at_least(uint32_t x) {
   return p;
 }
 
-int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g, const void* A, const void* B) {
+int32_t init_device(int dev, int& sm_count);
+
+// A launch with the in-cluster split-K sum asks for at least this much shared memory, so one CTA runs per SM: the
+// CTAs of a cluster then sit on distinct SMs and never wait on each other's tensor memory allocation.
+constexpr size_t kRedSmemFloor = kMaxSmemPerCta / 2 + 1024;
+// Clusters of 1..8 such CTAs that a B200 holds at once (cudaOccupancyMaxActiveClusters; used when no device is current)
+constexpr int kB200Clusters[9] = {0, 148, 74, 45, 33, 26, 22, 15, 15};
+
+// How many clusters of `size` CTAs of the lean kernel (E epilogue warps, one CTA per SM) fit on the current device at
+// once. Clusters live within a GPC, so this is below SMs / size (45 clusters of 3, 15 of 8 on a B200); a launch that
+// needs more runs a second wave of clusters, slower than the reduce kernel it replaces.
+int max_active_clusters(int epi_warps, int size) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return kB200Clusters[size];
+  }
+  static std::mutex mu;
+  static int cache[64][2][9];
+  static bool filled[64][2][9];
+  const int ei = epi_warps == 8 ? 1 : 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!filled[dev][ei][size]) {
+    int sms = 0, n = 0;
+    if (init_device(dev, sms) == B2G_OK) {
+      cudaLaunchConfig_t lc = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = static_cast<unsigned>(size);
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      lc.gridDim = dim3(static_cast<unsigned>(size), 1, 1);
+      lc.blockDim = dim3((2 + epi_warps) * 32, 1, 1);
+      lc.dynamicSmemBytes = kRedSmemFloor;
+      lc.attrs = attr;
+      lc.numAttrs = 1;
+      const cudaError_t e = ei ? cudaOccupancyMaxActiveClusters(&n, gemm_kernel<8, 0, 1>, &lc)
+                               : cudaOccupancyMaxActiveClusters(&n, gemm_kernel<4, 0, 1>, &lc);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+    }
+    cache[dev][ei][size] = n;
+    filled[dev][ei][size] = true;
+  }
+  return cache[dev][ei][size];
+}
+
+// allow_red: whether SPLIT_K may be summed inside a cluster (the allocation-free entry point keeps the workspace path).
+int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g, const void* A, const void* B,
+                      bool allow_red = true) {
   if (!cfg || !pr) return fail(B2G_ERR_INVALID_ARG, "null config or problem");
   if (pr->dtype != B2G_DTYPE_F16 && pr->dtype != B2G_DTYPE_BF16)
     return fail(B2G_ERR_INVALID_ARG, "dtype must be B2G_DTYPE_F16 or B2G_DTYPE_BF16");
@@ -1162,6 +1337,23 @@ int32_t make_geometry(const b2g_config* cfg, const b2g_problem* pr, Geometry& g,
     g.ws_partial = 0;
     sk_bytes = 0;
     g.a.pack = g.b.pack = 0;
+  }
+  // SPLIT_K of 2..8 on single-CTA tiles of at most 8192 outputs is summed inside a cluster of the tile's CTAs when
+  // every cluster of the launch fits on the GPU at once (one CTA per unit, one wave): each CTA keeps its fp32 partial in its own operand
+  // ring (free once the tile's MMAs are done) and the sum reads the peers' rings. Same split order as the reduce
+  // kernel, so the same bits, without the second launch or the partials' round trip through global memory.
+  g.red_cluster = 0;
+  if (allow_red && K > 0 && cfg->split_k >= 2 && cfg->split_k <= kMaxRedCluster && !g.pair && !g.streamk) {
+    const size_t red_bytes = static_cast<size_t>(g.tile_m + 4) * (g.tile_n + 4) * 4;
+    const size_t ring = stage * g.stages;
+    const int64_t clusters = static_cast<int64_t>(g.tiles_m) * g.tiles_n;
+    // Larger partials (128 x 128 tiles: 64 KB per CTA) measured 4-5 % slower summed this way than by the reduce
+    // kernel spread over every SM; decode-shaped and 128 x 64 tiles 3-16 % faster.
+    const bool small = static_cast<int64_t>(g.tile_m) * g.tile_n <= kMaxRedElems;
+    if (small && red_bytes <= ring && clusters <= max_active_clusters(g.epi_warps, cfg->split_k)) {
+      g.red_cluster = 1;
+      g.ws_partial = 0;
+    }
   }
   // workspace: [split-K partials][stream-K flags + slots][staged A][staged B]
   g.sk_flags_off += g.ws_partial;
@@ -1310,9 +1502,9 @@ int grid_for(int64_t work, int per_block) {
 
 // Fill `p` (caller-owned) with the launch plan of (cfg, prob) on the current device.
 int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, const void* A, const void* B, void* C,
-                  void* workspace, size_t workspace_bytes, int32_t* status) {
+                  void* workspace, size_t workspace_bytes, int32_t* status, bool allow_red = true) {
   Geometry g;
-  int32_t rc = make_geometry(cfg, prob, g, A, B);
+  int32_t rc = make_geometry(cfg, prob, g, A, B, allow_red);
   if (rc != B2G_OK) return rc;
   const int64_t M = prob->M, N = prob->N, K = prob->K;
   if ((M > 0 && N > 0) && (!C || (K > 0 && (!A || !B)))) return fail(B2G_ERR_INVALID_ARG, "null A, B or C");
@@ -1407,7 +1599,8 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
     k.sk_iters = g.sk_iters;
     k.sk_flags = g.streamk ? reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + g.sk_flags_off) : nullptr;
     k.sk_slots = g.streamk ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + g.sk_slots_off) : nullptr;
-    if (cfg->split_k > 1) {
+    k.red_cluster = g.red_cluster;
+    if (cfg->split_k > 1 && !g.red_cluster) {
       k.out = workspace;
       k.out_kind = OUT_F32_PARTIAL;
       k.out_split_stride = M * N;
@@ -1432,18 +1625,20 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
       k.out_si = g.swapped ? prob->stride_cn : prob->stride_cm;
       k.out_sj = g.swapped ? prob->stride_cm : prob->stride_cn;
       k.vec_ok = (k.out_sj == 1) && (k.out_si % 8 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+      // the cluster sum writes 8 outputs at a time along C's contiguous direction
+      k.red_imajor = (k.out_sj != 1 && k.out_si == 1) ? 1 : 0;
     }
     p->epi_warps = g.epi_warps;
     p->pair = g.pair;
     p->threads = (2 + g.epi_warps) * 32;
-    p->smem = g.smem;
+    p->smem = g.red_cluster ? std::max(g.smem, kRedSmemFloor) : g.smem;
     {
       // staged epilogue: row-major C (or the fp32 partials) in whole 16-byte pieces, 64-column half-precision chunk
       // pairs, and room for 4 KB per epilogue warp next to the ring
       const size_t staging = static_cast<size_t>(g.epi_warps) * 4096;
       const bool partial = cfg->split_k > 1;
       const bool pieces_ok = partial ? (N % 4 == 0) : (N % 8 == 0 && g.tile_n % 64 == 0);
-      if (!g.swapped && k.vec_ok && pieces_ok && g.smem + staging <= kMaxSmemPerCta) {
+      if (!g.swapped && !g.red_cluster && k.vec_ok && pieces_ok && g.smem + staging <= kMaxSmemPerCta) {
         k.stage_c = 1;
         k.epi_stage_off = static_cast<uint32_t>(static_cast<size_t>(g.cta_m + g.cta_n) * g.bk * 2 * g.stages);
         p->smem = g.smem + staging;
@@ -1510,6 +1705,8 @@ int32_t plan_init(b2g_plan* p, const b2g_config* cfg, const b2g_problem* prob, c
     }
     p->grid = static_cast<int>(std::max<int64_t>(grid, 1));
     p->lean = !g.pair && !g.streamk && grid == g.units;
+    if (g.red_cluster && !p->lean)
+      return fail(B2G_ERR_UNSUPPORTED, "cluster_split_k: the in-cluster split-K sum needs one CTA per (tile, split)");
   }
   p->user_a = A;
   p->user_b = B;
@@ -1681,6 +1878,13 @@ int32_t b2g_plan_launch(const b2g_plan* p, void* stream) {
     } else {
       lc.gridDim = dim3(p->grid, 1, 1);
       lc.numAttrs = 1;
+      if (p->kp.red_cluster) {  // the SPLIT_K CTAs of a tile (consecutive units) form one cluster
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = static_cast<unsigned>(p->kp.split_k);
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        lc.numAttrs = 2;
+      }
       if (p->lean)
         le = (p->epi_warps == 4) ? cudaLaunchKernelEx(&lc, gemm_kernel<4, 0, 1>, p->kp, p->tma_a, p->tma_b)
                                  : cudaLaunchKernelEx(&lc, gemm_kernel<8, 0, 1>, p->kp, p->tma_a, p->tma_b);
@@ -1810,7 +2014,7 @@ int32_t b2g_splitk_reduce(const float* ws, void* C, int64_t M, int64_t N, int64_
 int32_t b2g_gemm_noalloc(const b2g_config* cfg, const b2g_problem* prob, const void* A, const void* B, void* C,
                          int32_t* status, void* stream) {
   Geometry g;
-  int32_t rc = make_geometry(cfg, prob, g, A, B);
+  int32_t rc = make_geometry(cfg, prob, g, A, B, false);
   if (rc != B2G_OK) return rc;
   if (g.streamk)
     return fail(B2G_ERR_UNSUPPORTED,
@@ -1835,7 +2039,7 @@ int32_t b2g_gemm_noalloc(const b2g_config* cfg, const b2g_problem* prob, const v
   if (rc != B2G_OK) return rc;
   // Nothing in the scratch needs clearing: each call's GEMM writes every partial element its reduce then reads.
   b2g_plan plan;
-  rc = plan_init(&plan, cfg, prob, A, B, C, scratch, kNoAllocScratchBytes, status);
+  rc = plan_init(&plan, cfg, prob, A, B, C, scratch, kNoAllocScratchBytes, status, false);
   if (rc != B2G_OK) return rc;
   return b2g_plan_launch(&plan, stream);
 }

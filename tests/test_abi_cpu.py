@@ -68,17 +68,26 @@ def test_workspace_size():
     assert workspace_bytes(MatmulConfig(128, 128, 64), 512, 512, 512) == 0
     def r256(x):
         return -(-x // 256) * 256
-    # fp32 partials [4, 100, 70], then B staged: N = 70 is not a multiple of 8, so rows of 72 elements, K = 1000 rows.
-    # the second kernel sums the splits: the workspace is the partials (and any staged operand), nothing else
+    # SPLIT_K <= 8 on single-CTA tiles of at most 8192 outputs is summed inside a cluster of the tile's CTAs: no
+    # partials, only staged operands (B here: N = 70 is not a multiple of 8, so rows of 72 elements, K = 1000 rows)
+    assert workspace_bytes(MatmulConfig(128, 64, 64, SPLIT_K=4), 100, 70, 1000) == r256(1000 * 72 * 2)
+    assert workspace_bytes(MatmulConfig(128, 64, 64, SPLIT_K=4), 128, 64, 1024) == 0
+    assert workspace_bytes(MatmulConfig(16, 128, 128, num_stages=6, GROUP_M=1, SPLIT_K=4), 24, 1000, 2048) == 0
+    assert workspace_bytes(MatmulConfig(128, 64, 64, num_stages=6, GROUP_M=1, SPLIT_K=2), 512, 256, 2048) == 0
+    # otherwise the second kernel sums fp32 partials [SPLIT_K, M, N] from the workspace: larger tiles, more than 8
+    # splits, CTA pairs, and launches with more clusters than fit at once
     assert workspace_bytes(MatmulConfig(128, 128, 64, SPLIT_K=4), 100, 70, 1000) == r256(4 * 100 * 70 * 4) + r256(
         1000 * 72 * 2)
-    assert workspace_bytes(MatmulConfig(128, 128, 64, SPLIT_K=4), 128, 64, 1024) == r256(4 * 128 * 64 * 4)
-    assert workspace_bytes(MatmulConfig(16, 128, 128, num_stages=6, GROUP_M=1, SPLIT_K=4), 24, 1000, 2048) == r256(
-        4 * 24 * 1000 * 4)
-    assert workspace_bytes(MatmulConfig(128, 64, 64, num_stages=6, GROUP_M=1, SPLIT_K=2), 512, 256, 2048) == r256(
-        2 * 512 * 256 * 4)
+    assert workspace_bytes(MatmulConfig(128, 64, 64, SPLIT_K=16), 128, 64, 1024) == r256(16 * 128 * 64 * 4)
     assert workspace_bytes(MatmulConfig(256, 128, 64, num_stages=6, SPLIT_K=2, CLUSTER=2), 512, 256, 1024) == r256(
         2 * 512 * 256 * 4)
+    # the clusters of one launch must all fit on the GPU at once (33 clusters of 4 CTAs on a B200): 32 tiles do,
+    # 512 tiles would need further waves of clusters and keep the reduce kernel
+    assert workspace_bytes(MatmulConfig(128, 64, 64, SPLIT_K=4, PERSISTENT=0), 512, 512, 1024) == 0
+    assert workspace_bytes(MatmulConfig(128, 64, 64, SPLIT_K=4, PERSISTENT=0), 2048, 2048, 1024) == r256(
+        4 * 2048 * 2048 * 4)
+    # 16 tiles x 8 splits: more clusters of 8 than a B200 holds at once (15)
+    assert workspace_bytes(MatmulConfig(32, 256, 64, SPLIT_K=8), 1, 4096, 4096) == r256(8 * 1 * 4096 * 4)
     lib = _abi.load()
     n = ctypes.c_size_t()
     pr = _abi.Problem(M=17, N=33, K=65, stride_am=65, stride_ak=1, stride_bk=33, stride_bn=1, stride_cm=33,

@@ -279,26 +279,93 @@ def test_square_16384_properties():
 
 
 def test_split_k_plan_replays_from_a_cuda_graph():
-    """The split-K reduce is a programmatic dependent launch of the GEMM; a runner captured into a CUDA graph (as the
-    timer does) replays both kernels in order and gives the same bits as a direct call."""
-    cfg = MatmulConfig(128, 128, 64, num_stages=4, GROUP_M=1, SPLIT_K=4)
+    """Split-K runners captured into a CUDA graph (as the timer does) give the same bits as a direct call: one launch of
+    CTA clusters that sum the splits in shared memory, or (larger tiles, more than 8 splits) the GEMM and its reduce
+    kernel, a programmatic dependent launch."""
     a_cpu, b_cpu = oracle.make_inputs(192, 256, 2048, seed=9)
     a, b = a_cpu.cuda(), b_cpu.cuda()
-    run = B200Matmul(cfg).make_runner(a, b)
-    direct = run().clone()
-    side = torch.cuda.Stream()
-    side.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(side):
-        run()
-    torch.cuda.current_stream().wait_stream(side)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(side):
-        g.capture_begin()
-        run()
-        g.capture_end()
-    run.c.fill_(float("nan"))
-    g.replay()
+    ref = oracle.gemm_f32(a_cpu, b_cpu)
+    for cfg in (MatmulConfig(128, 64, 64, num_stages=4, GROUP_M=1, SPLIT_K=4),
+                MatmulConfig(128, 128, 64, num_stages=4, GROUP_M=1, SPLIT_K=4),
+                MatmulConfig(128, 64, 64, num_stages=4, GROUP_M=1, SPLIT_K=12)):
+        run = B200Matmul(cfg).make_runner(a, b)
+        assert run.num_kernels == (1 if cfg.SPLIT_K <= 8 and cfg.BLOCK_N == 64 else 2)
+        direct = run().clone()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            run()
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            g.capture_begin()
+            run()
+            g.capture_end()
+        run.c.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        run.raise_on_status()
+        assert torch.equal(run.c, direct)
+        _assert_parity(run.c, ref, a_cpu, b_cpu, 2048)
+        del g
+
+
+# (config, (M, N, K), dtype, C's leading-dimension padding, B transposed in memory): split-K summed inside CTA clusters
+CLUSTER_SPLITS = [
+    (MatmulConfig(128, 64, 64, num_stages=4, GROUP_M=1, SPLIT_K=4), (512, 384, 2048), torch.float16, 0, False),
+    (MatmulConfig(16, 128, 128, num_stages=6, GROUP_M=1, SPLIT_K=4), (24, 1000, 2048), torch.float16, 0, False),
+    (MatmulConfig(32, 256, 64, num_stages=6, GROUP_M=1, SPLIT_K=8), (1, 2048, 4096), torch.float16, 0, False),
+    (MatmulConfig(128, 64, 64, num_stages=6, GROUP_M=1, SPLIT_K=8), (256, 192, 256), torch.float16, 0, False),
+    (MatmulConfig(128, 64, 64, num_stages=4, GROUP_M=8, SPLIT_K=3), (300, 520, 1000), torch.bfloat16, 0, False),
+    (MatmulConfig(256, 32, 64, num_stages=4, GROUP_M=1, SPLIT_K=2), (512, 384, 2048), torch.float16, 0, True),
+    (MatmulConfig(128, 64, 128, num_stages=3, GROUP_M=1, SPLIT_K=5), (256, 256, 2560), torch.float16, 8, False),
+    (MatmulConfig(128, 64, 64, num_stages=6, GROUP_M=1, SPLIT_K=7, PERSISTENT=0), (200, 136, 3000), torch.float16,
+     0, True),
+    (MatmulConfig(64, 128, 64, num_stages=8, GROUP_M=1, SPLIT_K=6), (40, 264, 1536), torch.bfloat16, 16, False),
+]
+
+
+@pytest.mark.parametrize("case", range(len(CLUSTER_SPLITS)))
+def test_split_k_cluster_sum_matches_the_reduce_kernel(case):
+    """SPLIT_K <= 8 on tiles of at most 8192 outputs, with every cluster of the launch resident at once, runs as one
+    launch whose CTA clusters sum the splits through shared memory, in the split order of the separate reduce kernel. Its output must equal, bit for bit, the workspace path's
+    (the allocation-free entry point keeps that path: fp32 partials in its scratch, then the reduce kernel), and pass
+    both bounds. Cases cover ragged tiles, splits with empty K ranges (8 splits of 4 K blocks), the skinny swapped
+    form (C written along its columns), 256-row tiles, odd split counts, bf16, a padded C and a K-major B."""
+    import ctypes
+
+    from cs464_b200 import _abi
+    from cs464_b200.matmul import problem
+    cfg, (M, N, K), dt, pad, bt = CLUSTER_SPLITS[case]
+    a_cpu, b_cpu = oracle.make_inputs(M, N, K, dtype=dt, seed=30 + case)
+    a = a_cpu.cuda()
+    b = b_cpu.t().contiguous().cuda().t() if bt else b_cpu.cuda()  # K-major B: a transposed view
+    c_full = torch.full((M, N + pad), float("nan"), device="cuda", dtype=dt)
+    c = c_full[:, :N]
+    run = B200Matmul(cfg).make_runner(a, b, out=c)
+    assert run.num_kernels == 1, "expected the single-launch cluster sum"
+    run()
     torch.cuda.synchronize()
     run.raise_on_status()
-    assert torch.equal(run.c, direct)
-    _assert_parity(run.c, oracle.gemm_f32(a_cpu, b_cpu), a_cpu, b_cpu, 2048)
+    _assert_parity(c, oracle.gemm_f32(a_cpu, b_cpu), a_cpu, b_cpu, K)
+    assert torch.isnan(c_full[:, N:]).all(), "wrote outside C"
+    ref = torch.full_like(c_full, float("nan"))
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    lib = _abi.load()
+    pr = problem(M, N, K, a.stride(), b.stride(), ref[:, :N].stride(), dt)
+    rc = lib.b2g_gemm_noalloc(ctypes.byref(cfg.to_abi()), ctypes.byref(pr), a.data_ptr(), b.data_ptr(),
+                              ref.data_ptr(), status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == _abi.B2G_OK, _abi.last_error()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(c, ref[:, :N]), "cluster sum differs from the reduce kernel's bits"
+
+
+def test_split_k_beyond_one_wave_of_clusters_keeps_the_reduce_kernel():
+    """16 tiles x 8 splits need 16 clusters of 8 CTAs; a B200 holds 15 at once, so the plan keeps the GEMM + reduce
+    kernel pair (a second wave of clusters measured slower); the result is the same either way."""
+    cfg = MatmulConfig(32, 256, 64, num_stages=6, GROUP_M=1, SPLIT_K=8)
+    a_cpu, b_cpu = oracle.make_inputs(1, 4096, 4096, seed=41)
+    c, run = _run(cfg, a_cpu, b_cpu)
+    assert run.num_kernels == 2
+    _assert_parity(c, oracle.gemm_f32(a_cpu, b_cpu), a_cpu, b_cpu, 4096)

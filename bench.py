@@ -380,9 +380,9 @@ def _pin_to_gpu_numa_node(dev):
 def e2e_leg(args, work, dev, stream, barrier, max_over_ranks, flops_step: float, world: int) -> dict:
     """The sweep end to end through the public API (`cs464_b200.matmul`): every step copies each size's inputs from
     pinned host memory, multiplies, and copies the result back to pinned host memory. Copies in, GEMMs and copies out
-    run on three streams, so one size's copy back overlaps the next size's copy in and GEMM (a user pipelines the
-    same way); the caching allocator's record_stream keeps each buffer alive until every stream using it is done.
-    Timed on the device from the first copy in to the last copy out."""
+    run on three streams: the copies in stream back to back while earlier sizes' GEMMs and copies back proceed (a user
+    pipelines the same way); the caching allocator's record_stream keeps each buffer alive until every stream using
+    it is done. Timed on the device from the first copy in to the last copy out."""
     import torch
 
     from cs464_b200.matmul import matmul
@@ -401,7 +401,9 @@ def e2e_leg(args, work, dev, stream, barrier, max_over_ranks, flops_step: float,
 
     def e2e_step():
         for w, (ha, hb, hc) in zip(work, host):
-            s_in.wait_stream(stream)  # inputs may be allocated on memory the previous step's GEMM just released
+            # No wait on the GEMM stream here: the copies in run back to back (PCIe is the bound) while earlier GEMMs
+            # and copies out proceed. Memory an earlier step released is safe to reuse because every buffer is
+            # record_stream'ed on the streams that use it, so the caching allocator holds it until they are done.
             with torch.cuda.stream(s_in):
                 a = ha.to(dev, non_blocking=True)
                 b = hb.to(dev, non_blocking=True)

@@ -83,7 +83,7 @@ def parse_args():
     ap.add_argument("--search-shapes", type=int, default=SEARCH_SHAPES,
                     help="first N shapes of BASELINE config 5 for the sharded-search leg")
     ap.add_argument("--search-space", type=int, default=SEARCH_SPACE,
-                    help="configs screened per shape (strided over the shape-pruned space), plus the ranker's top 3")
+                    help="configs screened per shape (strided over the shape-pruned space), plus the selection's candidates")
     a = ap.parse_args()
     if a.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -233,8 +233,8 @@ def search_leg(args, rank: int, world: int, dev, barrier, max_over_ranks) -> dic
         return None
     s = shard.summarize(str(out), [{**stats, "wall_s": wall_max}], str(queue))
     return {"workload": f"BASELINE config 5, first {len(shapes)} of its 1000 fresh shapes (seed 2): per shape the "
-                        f"ranker's top 3 (validated + short-timed: the selection) and a screen of {args.search_space} "
-                        "configs strided over the shape-pruned space plus the top 3, cold L2",
+                        f"ranker's top 3 and the zero-search rule's config (validated + short-timed: the selection) and a "
+                        f"screen of {args.search_space} configs strided over the shape-pruned space plus those, cold L2",
             "shapes": s["shapes"], "units": s["units"], "ranks": world, "wall_s": round(wall_max, 3),
             "shapes_per_s": None if s["shapes_per_s"] is None else round(s["shapes_per_s"], 4),
             "gap_median": s["gap_median"], "gap_p95": s["gap_p95"], "crashed": s["crashed"],
@@ -465,7 +465,7 @@ def main():
     from cs464_b200.matmul import B200Matmul
     from cs464_b200.gate import reference
     from cs464_b200.ranker import default_ranker
-    from cs464_b200.search import FAMILY, choose, measure
+    from cs464_b200.search import FAMILY, choose, measure, selection_keys
     from cs464_b200.select import heuristic_config
 
     torch.cuda.set_device(local)
@@ -489,7 +489,7 @@ def main():
     def select_config(a, b):
         """First-use selection for one square size: ranker top 3 + the zero-search rule, short-timed."""
         n = a.shape[0]
-        keys = list(dict.fromkeys(ranker.rank(n, n, n, 3, order="diverse") + [heuristic_config(n, n, n).key()]))
+        keys = selection_keys(ranker, n, n, n, 3)
         r = measure(n, n, n, torch.float16, [(FAMILY, k, B200Matmul(parse_key(k))) for k in keys],
                     inputs=(a, b, reference(a, b)))
         choice = choose(r["candidates"])

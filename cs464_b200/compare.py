@@ -1,8 +1,8 @@
 """Per-shape comparison of the sm_100a family with cuBLASLt and torch.matmul (BASELINE.json configs 3 and 4).
 
 For every shape of a suite, on one GPU, with one timing protocol (cold L2, CUDA events, trimmed mean of the samples):
-  * `sel`   the family's zero-search pick: the ranker's top-k validated and short-timed, the fastest kept
-            (`search.search_shape` + `choose`), then re-timed with the full protocol;
+  * `sel`   the family's first-use pick: the ranker's top-k and the zero-search rule's config, validated and
+            short-timed, the fastest kept (`search.search_shape` + `choose`), then re-timed with the full protocol;
   * `best`  the family's best-in-pool over a screen of the shape-pruned space (`--space N` configs, 0 = skip);
   * `lt`    cuBLASLt's heuristic top-`lt_n`, each validated and timed: `lt0` = rank 0 (B2), `lt_best` = best (B3);
             with `--lt-deep-s S`, also the fastest configs of a budgeted search of cuBLASLt's configuration space
@@ -29,7 +29,7 @@ from cs464_b200.baselines import TorchMatmul
 from cs464_b200.gate import make_inputs, reference, validate
 from cs464_b200.keys import parse_key
 from cs464_b200.matmul import B200Matmul
-from cs464_b200.search import choose, measure, screen_shape, shape_space
+from cs464_b200.search import choose, measure, screen_shape, selection_keys, shape_space
 from cs464_b200.timing import Protocol, measure_us
 
 FULL = Protocol(mode="cold", samples=20, max_samples=100, warmup=3, ci_target=0.01, max_s=1.0)
@@ -52,7 +52,7 @@ def compare_shape(shape: dict, *, k: int = 3, space: int = 0, lt_n: int = 16, ra
     if ranker is None:
         from cs464_b200.search import _ranker_default
         ranker = _ranker_default()
-    keys = ranker.rank(M, N, K, k, order="diverse")
+    keys = selection_keys(ranker, M, N, K, k)
     sel = measure(M, N, K, dtype, [("b200_sm100a_v1", x, B200Matmul(parse_key(x))) for x in keys], inputs=(a, b, ref))
     choice = choose(sel["candidates"])
     row["select_s"] = time.perf_counter() - t0

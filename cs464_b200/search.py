@@ -214,12 +214,20 @@ def choose(cands: list[dict], k: int | None = None) -> dict:
             "mode": metric[:-3], "us": best.get("confirm_us", best[metric]), **cost}
 
 
+def selection_keys(ranker, M: int, N: int, K: int, k: int, order: str = "diverse") -> list[str]:
+    """The configs a first-use selection times: the ranker's top k and the zero-search rule's config (when it is not
+    among them). The rule covers what the ranker's training data predates (e.g. decode split counts whose clusters fit
+    the GPU at once)."""
+    from cs464_b200.select import heuristic_config
+    ranker = ranker or _ranker_default()
+    return list(dict.fromkeys(list(ranker.rank(M, N, K, k, order=order)) + [heuristic_config(M, N, K).key()]))
+
+
 def search_shape(ranker, M: int, N: int, K: int, k: int, dtype=torch.float16, order: str = "diverse",
                  confirm: int = 0) -> dict:
-    """Rank, then validate + short-time the top k."""
-    ranker = ranker or _ranker_default()
+    """Rank, then validate + short-time the top k and the zero-search rule's config."""
     t0 = time.perf_counter()
-    keys = ranker.rank(M, N, K, k, order=order)
+    keys = selection_keys(ranker, M, N, K, k, order=order)
     rank_s = time.perf_counter() - t0
     backends = [(FAMILY, key, B200Matmul(parse_key(key))) for key in keys]
     r = measure(M, N, K, dtype, backends, confirm=confirm)
@@ -230,7 +238,8 @@ def select_kernel(ranker, M: int, N: int, K: int, *, calls: int | None = None, f
                   policy: KPolicy = KPolicy(), dtype=torch.float16, cache=True, confirm: int = 0,
                   serve_stale: bool = False, extra=None) -> dict:
     """First-use selection for one shape: a cached winner from a search at least this wide is returned without any
-    GPU work; otherwise the ranker's top k are validated and timed, the fastest is stored and returned.
+    GPU work; otherwise the ranker's top k and the zero-search rule's config are validated and timed, the fastest is
+    stored and returned.
     Returns {"k", "reason", "choice", "candidates", "rank_s", "cached"}."""
     import warnings
 

@@ -329,7 +329,7 @@ def search_unit(shape: dict, unit: dict, *, k: int = 3, space: int | None = None
     from cs464_b200.gate import make_inputs, reference
     from cs464_b200.keys import parse_key
     from cs464_b200.matmul import B200Matmul
-    from cs464_b200.search import FAMILY, choose, measure, screen_shape
+    from cs464_b200.search import FAMILY, choose, measure, screen_shape, selection_keys
     M, N, K = shape["M"], shape["N"], shape["K"]
     t0 = time.perf_counter()
     if ranker is None:
@@ -338,7 +338,7 @@ def search_unit(shape: dict, unit: dict, *, k: int = 3, space: int | None = None
     a, b = make_inputs(M, N, K, torch.float16, scale_b=shape.get("weight_std", 1.0))
     ref = reference(a, b)
     t_rank = time.perf_counter()
-    top = ranker.rank(M, N, K, k, order="diverse")
+    top = selection_keys(ranker, M, N, K, k)
     t_rank = time.perf_counter() - t_rank
     row = {"i": unit["i"], "slice": unit["slice"], "of": unit["of"], "M": M, "N": N, "K": K, "top": top,
            "crashed": sorted(crashed), "rank_s": t_rank}

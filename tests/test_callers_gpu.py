@@ -107,12 +107,13 @@ def test_gate_keeps_a_slow_host_out_of_the_samples():
 def test_select_kernel_searches_then_hits_the_cache(tmp_path):
     wc = WinnerCache(tmp_path / "wc.jsonl", env=environment())
     r1 = select_kernel(None, 777, 512, 1024, cache=wc)
-    assert not r1["cached"] and r1["choice"]["key"] is not None and len(r1["candidates"]) == 3
+    # the ranker's top 3 and the zero-search rule's config (unless the ranker already proposed it)
+    assert not r1["cached"] and r1["choice"]["key"] is not None and len(r1["candidates"]) in (3, 4)
     assert all(c["valid"] for c in r1["candidates"]), r1["candidates"]
     r2 = select_kernel(None, 777, 512, 1024, cache=wc)
     assert r2["cached"] and r2["choice"]["key"] == r1["choice"]["key"]
     r3 = select_kernel(None, 777, 512, 1024, cache=wc, frequent=True)  # wider search than the cached one: searched
-    assert not r3["cached"] and len(r3["candidates"]) == 5
+    assert not r3["cached"] and len(r3["candidates"]) in (5, 6)
 
 
 def test_screen_shape_small_pool():
